@@ -1,0 +1,180 @@
+/*
+ * tilequant_b200 -- C ABI of the B200 (sm_100a) mixed-precision 64x64 tile GEMM path.
+ *
+ * Drop-in boundary for the reference's Triton path (HanzhiZhang-Ulrica/TileQuant,
+ * src/kernels/triton/ and the torch paths of src/kernels/quant_utils.py and
+ * src/kernels/pack.py).  Every entry point takes plain device pointers, element
+ * strides and a cudaStream_t passed as void*; nothing here allocates device memory.
+ * All kernels are asynchronous on `stream` and may be captured in a CUDA graph.
+ *
+ * Return value: TQ_OK (0) or a TQ_ERR_* code; tq_last_error() gives a message for
+ * the calling thread's last failure.  Shape/argument problems are detected on the
+ * host before any launch.  Device-side waits are bounded: a wait that gives up
+ * writes TQ_ERR_TIMEOUT into the optional `err` word (a device int the caller
+ * zeroes and reads back) instead of hanging.
+ *
+ * Tile layout (the reference's Pack, src/kernels/pack.py:11-29, unchanged):
+ *   tile id = r * n_tc + c for the 64x64 tile at output rows [64r, 64r+64) and input
+ *   columns [64c, 64c+64) of the zero-padded weight W (M_pad x K_pad);
+ *   int8_tiles  int8[T8][64][64], tile[i][j] = W[64r+i][64c+j] quantized;
+ *   int8_scales f32[T8];  int8_tile_ids int32[T8] ascending;  int8_row_ptr int32[n_tr+1];
+ *   fp16_tiles  bf16/f16[T16][64][64]; fp16_tile_ids int32[T16]; fp16_row_ptr int32[n_tr+1].
+ */
+#ifndef TILEQUANT_B200_H
+#define TILEQUANT_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TQ_API __attribute__((visibility("default")))
+#else
+#define TQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  TQ_OK = 0,
+  TQ_ERR_INVALID = 1,     /* bad shape / stride / dtype / alignment argument      */
+  TQ_ERR_UNSUPPORTED = 2, /* valid request this build does not implement          */
+  TQ_ERR_CUDA = 3,        /* a CUDA runtime call failed                           */
+  TQ_ERR_TIMEOUT = 4      /* written to the device error word by a bounded wait   */
+};
+
+enum { TQ_DTYPE_BF16 = 0, TQ_DTYPE_F16 = 1 };
+
+enum {
+  TQ_ALGO_AUTO = 0,  /* pick by problem shape                                     */
+  TQ_ALGO_ROWS = 1,  /* split-K row-owned kernel: bulk-copy weight stream, cluster
+                        (DSMEM) split reduction; decode and general fallback      */
+  TQ_ALGO_UMMA = 2   /* persistent TMA + tcgen05 (kind::i8 / kind::f16) kernel    */
+};
+
+/* ABI version of this header (bumped on any signature change). */
+TQ_API int tq_abi_version(void);
+
+/* Message for the calling thread's last non-OK return. */
+TQ_API const char* tq_last_error(void);
+
+/* Static name of a status code. */
+TQ_API const char* tq_status_string(int status);
+
+/* ---------------------------------------------------------------- quantizer
+ * x is (n_rows, k) of x_dtype with element strides (ld_row, ld_col).
+ * sx[c] = f32(dtype(f32(absmax(x[:, 64c:64c+64])) / 127)), 1.0 for an all-zero
+ * column tile; q = clamp(rint(f32(x) / sx[col/64]), -127, 127), contiguous rows of
+ * stride ldq (>= k).
+ */
+
+/* replaces activation_tile_absmax_scales (src/kernels/quant_utils.py:41-74) and the
+ * Triton _activation_tile_absmax_scales_64_kernel (triton/quantize_activation.py:13-44,
+ * host :158-176). */
+TQ_API int tq_act_scales(const void* x, int x_dtype, int64_t n_rows, int64_t k, int64_t ld_row, int64_t ld_col,
+                  float* sx, void* stream);
+
+/* replaces quantize_activation_tile_with_scales (src/kernels/quant_utils.py:78-115) and
+ * _quantize_activation_with_scales_64_kernel (triton/quantize_activation.py:47-74,
+ * host :179-203). */
+TQ_API int tq_quantize_with_scales(const void* x, int x_dtype, int64_t n_rows, int64_t k, int64_t ld_row,
+                            int64_t ld_col, const float* sx, int8_t* q, int64_t ldq, void* stream);
+
+/* replaces quantize_activation_tile_absmax (src/kernels/quant_utils.py:119-134) and the
+ * one-pass _quantize_activation_64_kernel (triton/quantize_activation.py:77-112,
+ * host :118-155); any n_rows. */
+TQ_API int tq_quantize_act(const void* x, int x_dtype, int64_t n_rows, int64_t k, int64_t ld_row, int64_t ld_col,
+                    int8_t* q, int64_t ldq, float* sx, void* stream);
+
+/* ---------------------------------------------------------------- mixed GEMM
+ * out[n, o] for n < n_rows, o < m (out features), k in features:
+ *   per row tile r and split s (of split_k), INT8 tiles in ascending column order:
+ *     acc = acc + f32(i32 tile dot) * (sx[c] * sw[t])   (separately rounded mul, add)
+ *   then BF16/F16 tiles: acc += f32 dot(x_fp tile, W tile);
+ *   split partials summed in split order; out = dtype(acc); with bias:
+ *   out = dtype(f32(out) + f32(bias[o])).
+ * x_i8 (n_rows, k) row stride ld_x8 bytes; x_fp (n_rows, k) of fp_dtype (the dtype of
+ * the 16-bit tiles too), row stride ld_xfp elements (may be NULL when t16 == 0);
+ * out (n_rows, m) of out_dtype, row stride ldo; bias (m) of out_dtype or NULL.
+ * split_k: 0 = automatic, else 1..16 (the result depends on split_k exactly as the
+ * reference's does).  algo: TQ_ALGO_*.  err: optional device error word.
+ *
+ * replaces gemm_mixed_rows_splitk / _gemm_mixed_rows_splitk_kernel
+ * (src/kernels/triton/gemm_rows_splitk_64x64.py:78-190, host :225-323).
+ */
+TQ_API int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
+                  const float* int8_scales, const int32_t* int8_tile_ids, const int32_t* int8_row_ptr,
+                  int64_t t8, const void* x_fp, int64_t ld_xfp, const void* fp16_tiles,
+                  const int32_t* fp16_tile_ids, const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype,
+                  void* out, int64_t ldo, int out_dtype, const void* bias, int64_t n_rows, int64_t m, int64_t k,
+                  int n_tr, int n_tc, int split_k, int algo, int* err, void* stream);
+
+/* Decode form with the activation quantizer fused into the GEMM prologue: the same
+ * result as tq_quantize_act followed by tq_gemm_mixed, in one launch.  n_rows <= 64.
+ * replaces quantize_activation_tile_absmax + gemm_mixed_rows_splitk as called by
+ * MixedLinear.forward for small row counts (src/models/mixed_linear.py:232-239). */
+TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dtype, const int8_t* int8_tiles,
+                              const float* int8_scales, const int32_t* int8_tile_ids,
+                              const int32_t* int8_row_ptr, int64_t t8, const void* fp16_tiles,
+                              const int32_t* fp16_tile_ids, const int32_t* fp16_row_ptr, int64_t t16,
+                              void* out, int64_t ldo, int out_dtype, const void* bias, int64_t n_rows, int64_t m,
+                              int64_t k, int n_tr, int n_tc, int split_k, int* err, void* stream);
+
+/* Launch geometry the split-K row kernel (TQ_ALGO_ROWS) uses when split_k = 0 on this
+ * device: *split (1..16) and *rows_per_cta (row tiles one CTA streams when split is 1).
+ * The split fixes the FP32 summation order of the result; passing it back as split_k
+ * reproduces the same result.  (The reference picks its split from a fixed rule,
+ * select_split_k, gemm_rows_splitk_64x64.py:52-67; this one sizes the grid to one
+ * wave of resident CTAs on the B200.) */
+TQ_API int tq_gemm_rows_plan(int64_t n_rows, int n_tr, int n_tc, int fp_dtype, int fused, int* split,
+                             int* rows_per_cta);
+
+/* Debug: the exact INT32 tile products the GEMM kernels form, partials[t][n][j] =
+ * sum_k x_i8[n, 64c+k] * int8_tiles[t][j][k] for every INT8 tile t (int32[t8][n_rows][64]).
+ * The reference computes the same value inside its kernel (gemm_rows_splitk_64x64.py:134)
+ * without exposing it. */
+TQ_API int tq_gemm_int8_partials(const int8_t* x_i8, int64_t ld_x8, const int8_t* int8_tiles,
+                          const int32_t* int8_tile_ids, const int32_t* int8_row_ptr, int64_t t8,
+                          int64_t n_rows, int64_t k, int n_tr, int n_tc, int32_t* partials, int algo,
+                          void* stream);
+
+/* ---------------------------------------------------------------- packer
+ * W (m, k) of w_dtype, row stride ldw elements, zero padded to (64 n_tr, 64 n_tc).
+ */
+
+/* INT8 codes and scales of the tiles `ids` (sorted): scale = f32(absmax)/127 (1.0 for
+ * an all-zero tile); with col_importance (f32[64 n_tc], may be NULL) the IAA search
+ * over {0.75, 1.0, 1.25} x scale by importance-weighted squared error, first best kept.
+ * replaces src/kernels/pack.py:119-167 (inside _pack_weight_with_tile_ids :65-203). */
+TQ_API int tq_pack_int8_tiles(const void* w, int w_dtype, int64_t m, int64_t k, int64_t ldw, int n_tc,
+                       const int32_t* ids, int64_t t8, const float* col_importance, int8_t* tiles,
+                       float* scales, void* stream);
+
+/* Gather the 16-bit tiles `ids` unchanged (zero padded).  replaces pack.py:172-177. */
+TQ_API int tq_gather_fp_tiles(const void* w, int w_dtype, int64_t m, int64_t k, int64_t ldw, int n_tc,
+                       const int32_t* ids, int64_t t16, void* tiles, void* stream);
+
+/* ---------------------------------------------------------------- calibration */
+
+/* tile_scores[r, c] += sum over the tile of |f32(W) * f32(G)| (f32 [n_tr][n_tc]).
+ * replaces the GI reduction of collect_gi_tile_scores (src/kernels/calibrate.py:153-164). */
+TQ_API int tq_calib_gi_accumulate(const void* w, const void* g, int dtype, int64_t m, int64_t k, int64_t ldw,
+                           int64_t ldg, int n_tr, int n_tc, float* tile_scores, void* stream);
+
+/* act_sum[j] += sum over rows of |f32(x[i, j])| accumulated in f64.
+ * replaces the IAA forward pre-hook (src/kernels/calibrate.py:244-255). */
+TQ_API int tq_calib_iaa_channel_accumulate(const void* x, int dtype, int64_t rows, int64_t k, int64_t ld_row,
+                                    double* act_sum, void* stream);
+
+/* mean[j] = f32(act_sum[j] / count); tile_scores[r, c] = sum over the tile of
+ * |f32(W)| * mean[col] (f32 [n_tr][n_tc]).
+ * replaces src/kernels/calibrate.py:346-367. */
+TQ_API int tq_calib_iaa_tile_scores(const void* w, int dtype, int64_t m, int64_t k, int64_t ldw,
+                             const double* act_sum, int64_t count, float* mean, float* tile_scores,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEQUANT_B200_H */

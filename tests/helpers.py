@@ -1,0 +1,61 @@
+"""Comparison helpers shared by the tests (bit patterns, BF16 ulp distance)."""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def ordered16(bits: np.ndarray) -> np.ndarray:
+    """Map 16-bit float bit patterns to integers that are monotonic in value."""
+    b = np.asarray(bits, np.uint16).astype(np.int32)
+    return np.where(b & 0x8000, 0x8000 - b, b)
+
+
+def ulp_dist16(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    return np.abs(ordered16(a_bits) - ordered16(b_bits))
+
+
+def assert_within_ulp(a_bits, b_bits, ulp: int = 1, what: str = ""):
+    d = ulp_dist16(a_bits, b_bits)
+    worst = int(d.max()) if d.size else 0
+    assert worst <= ulp, f"{what}: max BF16 ulp distance {worst} > {ulp} ({int((d > ulp).sum())} elements)"
+    return d
+
+
+def to_torch16(bits: np.ndarray, dtype, device=None):
+    """uint16 bit pattern -> 16-bit float tensor (no value conversion)."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(dtype)
+    return t.to(device) if device is not None else t
+
+
+def from_torch16(t) -> np.ndarray:
+    import torch
+
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def f16bits_to_f32(bits, dtype_code: int = 0) -> np.ndarray:
+    b = np.asarray(bits, np.uint16)
+    if dtype_code == 0:
+        return (b.astype(np.uint32) << 16).view(np.float32)
+    return b.view(np.float16).astype(np.float32)
+
+
+def ulp_bf16(v: np.ndarray) -> np.ndarray:
+    """Size of one BF16 ulp at |v| (8 significant bits)."""
+    a = np.maximum(np.abs(v).astype(np.float64), 1e-30)
+    return np.exp2(np.floor(np.log2(a)) - 7)
+
+
+def assert_close_with_bias(y_bits, ref_bits, bias_bits, what: str = "", dtype_code: int = 0):
+    """Outputs with bias: out = round(f32(round(acc)) + bias) rounds twice, so one ulp
+    of the pre-bias value can be many ulps of a cancelled sum.  Allowed error: one ulp
+    of the pre-bias value plus one ulp of the result."""
+    y = f16bits_to_f32(y_bits, dtype_code)
+    r = f16bits_to_f32(ref_bits, dtype_code)
+    b = f16bits_to_f32(bias_bits, dtype_code)[None, :]
+    tol = ulp_bf16(r - b) + ulp_bf16(r)
+    bad = np.abs(y - r) > tol
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond one pre-bias ulp"

@@ -1,0 +1,78 @@
+"""The C-ABI library loads, exports every entry point the header declares, and
+rejects bad arguments on the host (no GPU needed)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tilequant_b200 import _native as N
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "tilequant_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return re.findall(r"^TQ_API\s+(?:const\s+)?\w+\**\s+(tq_\w+)\s*\(", text, flags=re.M)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not N.LIB_PATH.exists():
+        from tilequant_b200 import build
+
+        build.build()
+    return N.load()
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert len(names) >= 14
+    assert set(names) == set(N.SIGNATURES), "ctypes table and header disagree"
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in _declared():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.tq_abi_version() == N.ABI_VERSION
+    assert lib.tq_status_string(N.TQ_ERR_INVALID) == b"TQ_ERR_INVALID"
+    assert lib.tq_status_string(N.TQ_ERR_TIMEOUT) == b"TQ_ERR_TIMEOUT"
+
+
+def test_host_side_argument_checks(lib):
+    # bad dtype / shapes are rejected before any CUDA call
+    assert lib.tq_act_scales(None, 7, 4, 64, 64, 1, None, None) == N.TQ_ERR_INVALID
+    assert b"dtype" in lib.tq_last_error()
+    assert lib.tq_quantize_act(None, 0, -1, 64, 64, 1, None, 64, None, None) == N.TQ_ERR_INVALID
+    # tile grid that does not match (m, k)
+    rc = lib.tq_gemm_mixed(None, 64, None, None, None, None, None, 0, None, 64, None, None, None, 0, 0, None, 64,
+                           0, None, 1, 64, 64, 2, 1, 0, 0, None, None)
+    assert rc == N.TQ_ERR_INVALID and b"tile grid" in lib.tq_last_error()
+    # tile counts that do not cover the grid
+    rc = lib.tq_gemm_mixed(None, 64, None, None, None, None, None, 3, None, 64, None, None, None, 0, 0, None, 64,
+                           0, None, 1, 64, 64, 1, 1, 0, 0, None, None)
+    assert rc == N.TQ_ERR_INVALID
+    # split_k beyond 16
+    dummy = ctypes.c_void_p(16)
+    rc = lib.tq_gemm_mixed(dummy, 64, dummy, dummy, dummy, dummy, dummy, 1, None, 64, None, None, None, 0, 0, dummy, 64,
+                           0, None, 1, 64, 64, 1, 1, 17, 0, None, None)
+    assert rc == N.TQ_ERR_INVALID and b"split_k" in lib.tq_last_error()
+    # fused decode form is limited to 64 rows
+    rc = lib.tq_gemm_mixed_fused_quant(dummy, 64, 0, dummy, dummy, dummy, dummy, 1, None, None, None, 0, dummy, 64, 0,
+                                       None, 65, 64, 64, 1, 1, 0, None, None)
+    assert rc == N.TQ_ERR_INVALID
+    assert lib.tq_calib_iaa_tile_scores(dummy, 0, 64, 64, 64, dummy, 0, dummy, dummy, None) == N.TQ_ERR_INVALID
+
+
+def test_python_errors_map_to_reference_exceptions(lib):
+    with pytest.raises(ValueError):
+        N.check(N.TQ_ERR_INVALID, "x")
+    with pytest.raises(N.TileQuantError):
+        N.check(N.TQ_ERR_CUDA, "x")

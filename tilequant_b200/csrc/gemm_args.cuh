@@ -1,0 +1,37 @@
+// Launch arguments shared by the mixed tile GEMM kernels.
+#pragma once
+
+#include <stdint.h>
+
+namespace tq {
+
+struct RowsArgs {
+  const int8_t* x_i8;  // (n_rows, K) INT8 activations, row stride ld_x8 bytes
+  int64_t ld_x8;
+  const float* sx;     // f32[n_tc] activation scales
+  const int8_t* w8;    // int8[T8][64][64]
+  const float* s8;     // f32[T8]
+  const int32_t* ids8;
+  const int32_t* rp8;
+  const void* x_fp;    // (n_rows, K) 16-bit activations, row stride ld_xfp elements
+  int64_t ld_xfp;
+  const void* w16;     // 16-bit [T16][64][64]
+  const int32_t* ids16;
+  const int32_t* rp16;
+  void* out;           // (n_rows, M) 16-bit, row stride ldo; null = no output
+  int64_t ldo;
+  int out_dtype;       // TQ_DTYPE_* of out and bias
+  const void* bias;
+  int32_t* partials;   // debug dump of INT32 tile products, or null
+  int* err;            // device error word, or null
+  int n_rows, M, K, n_tc, split;
+  int n_tr;            // row tiles of the weight
+  int rows_per_cta;    // row tiles one CTA streams (rows kernel, split 1)
+  int has_fp16;
+  int a8_vec;          // x_i8 rows are 16-byte addressable
+  int afp_vec;         // x_fp rows are 16-byte addressable
+  int fused;           // quantize x_fp in the kernel (x_i8 / sx unused)
+  int tma_x;           // activation tensor maps are valid (set by the launcher)
+};
+
+}  // namespace tq
