@@ -1,0 +1,504 @@
+#!/usr/bin/env python
+"""Benchmark of the mixed INT8/BF16 64x64 tile GEMM path on B200 (one JSON line).
+
+Workload (default, benchmark config 2): one Llama-3.2-3B decoder block at prefill,
+4 x 2048 tokens (8192 activation rows), hidden 3072, intermediate 8192, 24/8 heads,
+head_dim 128; random-init BF16 weights N(0, 0.02) with 5 % of each linear's 64x64
+tiles kept BF16 (uniformly chosen), the rest INT8 with one scale per tile.
+
+* a step = one pass of the hot path over the block: the four MixedLinear forwards
+  (stacked Q/K/V, O, stacked gate/up, down), each = activation quantization + mixed
+  GEMM, on the block's own activations (captured from one eager block forward);
+* ``value`` = linear ops of the block (2 * rows * sum(out * in) = 1.649e12) / step
+  time, TOPS; device time from CUDA events, L2 flushed (256 MB write) between steps;
+* ``e2e`` = the same metric for the whole block forward through the public module
+  API with the hidden states copied in from pinned host memory and the block output
+  copied back every step;
+* ``roofline`` = the dominant kernel (the stacked gate/up mixed GEMM) against the
+  dense INT8 peak measured in this run (cuBLASLt INT8 8192^3 via ``torch._int_mm``);
+* ``cpu_baseline`` = the CPU restatement of the reference (oracle/, C + OpenMP) on a
+  bounded sample of the same rows.
+
+``--impl reference`` times that CPU restatement alone: the reference's own GEMM is a
+Triton GPU kernel that needs the reference checkout, and its CPU torch path covers
+only the quantizer and the packer.  ``--workload decode`` measures config 1 (one
+q_proj-shaped MixedLinear, 16 decode tokens) in GB/s instead.
+
+Multi-GPU (torchrun): every rank runs its own replica of the workload (weak scaling);
+the step time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+import torch.nn.functional as F
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LLAMA3B = dict(hidden=3072, inter=8192, heads=24, kv_heads=8, head_dim=128, rope_theta=500000.0)
+TOKENS = (4, 2048)
+KEEP = 0.05
+METRIC_PREFILL = "tile-GEMM TOPS: Llama-3.2-3B decoder block prefill (4x2048 tokens), 4 MixedLinear forwards"
+
+
+def _peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+# ---------------------------------------------------------------- workload pieces
+
+def _cfg():
+    return SimpleNamespace(tile_m=64, tile_n=64, pad_to_tile=True, quant_style="gi", dtype_out="bf16")
+
+
+def _mixed_linear(out_f, in_f, seed, device, keep=KEEP):
+    import tilequant_b200 as tq
+    from tests.golden import inputs as I
+
+    w = I.weight(out_f, in_f, seed).to(device)
+    n_tr, n_tc = (out_f + 63) // 64, (in_f + 63) // 64
+    fp16 = I.keep_ids(n_tr, n_tc, keep, seed + 1)
+    pack = tq.pack_weight_from_tile_ids(w, n_tr=n_tr, n_tc=n_tc, int8_tile_ids=I.complement_ids(fp16, n_tr * n_tc),
+                                        fp16_tile_ids=fp16, cfg=_cfg())
+    return tq.MixedLinear(pack, None, _cfg())
+
+
+class Block:
+    """Llama decoder block with MixedLinear projections (RMSNorm, RoPE, causal GQA
+    SDPA, SwiGLU), Q/K/V and gate/up stacked into one GEMM each."""
+
+    def __init__(self, seed, device, dims=LLAMA3B, keep=KEEP):
+        import tilequant_b200 as tq
+
+        h, i, nh, nkv, hd = dims["hidden"], dims["inter"], dims["heads"], dims["kv_heads"], dims["head_dim"]
+        self.dims = dims
+        lin = lambda o, k, s: _mixed_linear(o, k, seed * 100 + s, device, keep)  # noqa: E731
+        self.qkv = tq.MixedLinearGroup([lin(nh * hd, h, 1), lin(nkv * hd, h, 3), lin(nkv * hd, h, 5)]).linear
+        self.o = lin(h, nh * hd, 7)
+        self.gate_up = tq.MixedLinearGroup([lin(i, h, 9), lin(i, h, 11)]).linear
+        self.down = lin(h, i, 13)
+        self.ln1 = torch.ones(h, device=device, dtype=torch.bfloat16)
+        self.ln2 = torch.ones(h, device=device, dtype=torch.bfloat16)
+        inv = 1.0 / (dims["rope_theta"] ** (torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd))
+        ang = torch.outer(torch.arange(TOKENS[1], device=device, dtype=torch.float32), inv)
+        self.cos = torch.cat([ang, ang], -1).cos().to(torch.bfloat16)
+        self.sin = torch.cat([ang, ang], -1).sin().to(torch.bfloat16)
+
+    @staticmethod
+    def _rms(x, w, eps=1e-5):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+
+    def _rope(self, x):  # (B, H, S, D)
+        d = x.shape[-1] // 2
+        return x * self.cos + torch.cat([-x[..., d:], x[..., :d]], -1) * self.sin
+
+    def forward(self, hidden, capture=None):
+        d = self.dims
+        B, S = TOKENS
+        nh, nkv, hd = d["heads"], d["kv_heads"], d["head_dim"]
+        x = self._rms(hidden, self.ln1)
+        q, k, v = self.qkv(x).split([nh * hd, nkv * hd, nkv * hd], dim=-1)
+        q = self._rope(q.view(B, S, nh, hd).transpose(1, 2))
+        k = self._rope(k.view(B, S, nkv, hd).transpose(1, 2))
+        v = v.view(B, S, nkv, hd).transpose(1, 2)
+        attn = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        attn = attn.transpose(1, 2).reshape(B * S, nh * hd)
+        h2 = hidden + self.o(attn)
+        x2 = self._rms(h2, self.ln2)
+        g, u = self.gate_up(x2).chunk(2, dim=-1)
+        act = (F.silu(g.float()) * u.float()).to(torch.bfloat16)
+        out = h2 + self.down(act)
+        if capture is not None:
+            capture.update(x_qkv=x, x_o=attn.contiguous(), x_gu=x2, x_down=act)
+        return out
+
+    def linear_ops(self, rows):
+        d = self.dims
+        h, i, nh, nkv, hd = d["hidden"], d["inter"], d["heads"], d["kv_heads"], d["head_dim"]
+        return 2 * rows * ((nh + 2 * nkv) * hd * h + h * nh * hd + 2 * i * h + h * i)
+
+
+# -------------------------------------------------------------------- helpers
+
+class ClockSampler:
+    """Polls SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index, period=0.01):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.handle, self.nvml.NVML_CLOCK_SM))
+                mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def _dist():
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+
+
+def _max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _int8_peak(device):
+    """cuBLASLt INT8 GEMM 8192^3 through torch._int_mm: best of 5, TOPS."""
+    try:
+        a = torch.randint(-127, 127, (8192, 8192), device=device, dtype=torch.int8)
+        b = torch.randint(-127, 127, (8192, 8192), device=device, dtype=torch.int8).t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = 0.0
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = max(best, 2 * 8192 ** 3 / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        return best, "measured in this run: torch._int_mm (cuBLASLt) INT8 8192^3, best of 5"
+    except Exception as exc:  # pragma: no cover - depends on the box
+        return 4500.0, f"datasheet dense INT8 (torch._int_mm failed: {type(exc).__name__})"
+
+
+def _cpu_sample(acts, block, rows):
+    """The CPU restatement of the reference (oracle/) on `rows` rows of each linear
+    input: quantize + mixed GEMM.  Returns (seconds, ops)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    t_total, ops = 0.0, 0
+    for name, mod in (("x_qkv", block.qkv), ("x_o", block.o), ("x_gu", block.gate_up), ("x_down", block.down)):
+        xb = acts[name][:rows].contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+        pk = {}
+        for key in ("int8_tiles", "int8_scales", "int8_tile_ids", "int8_row_ptr", "fp16_tiles", "fp16_tile_ids",
+                    "fp16_row_ptr"):
+            v = getattr(mod, key).cpu()
+            pk[key] = v.view(torch.int16).numpy().view(np.uint16) if v.dtype == torch.bfloat16 else v.numpy()
+        pk.update(n_tr=mod.n_tr, n_tc=mod.n_tc)
+        t0 = time.perf_counter()
+        q, sx = O.quantize_act(xb)
+        O.gemm(q, sx, pk, xb, mod.M_orig, mod.K_orig, split_k=1)
+        t_total += time.perf_counter() - t0
+        ops += 2 * rows * mod.M_orig * mod.K_orig
+    return t_total, ops
+
+
+def _prefill_setup(device):
+    from tests.golden import inputs as I
+
+    block = Block(seed=7, device=device)
+    rows = TOKENS[0] * TOKENS[1]
+    hidden = I.activations(rows, LLAMA3B["hidden"], 42).to(device)
+    acts = {}
+    with torch.inference_mode():
+        block.forward(hidden, capture=acts)
+    torch.cuda.synchronize()
+    return block, hidden, acts, rows
+
+
+# ----------------------------------------------------------------- workloads
+
+def run_prefill(args, ws, rank, device):
+    import tilequant_b200 as tq
+    from tilequant_b200 import _native as N
+
+    block, hidden, acts, rows = _prefill_setup(device)
+    flush = torch.empty(int(256e6) // 4, device=device, dtype=torch.float32)  # > 2x the 126 MB L2
+    ops = block.linear_ops(rows)
+
+    def step():
+        block.qkv(acts["x_qkv"])
+        block.o(acts["x_o"])
+        block.gate_up(acts["x_gu"])
+        block.down(acts["x_down"])
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        torch.cuda.synchronize()
+        launches0 = N.kernel_launches()
+        evs = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(args.steps)]
+        with ClockSampler(device.index) as clocks:
+            for e0, e1 in evs:
+                flush.zero_()
+                e0.record()
+                step()
+                e1.record()
+            torch.cuda.synchronize()
+        launches = N.kernel_launches() - launches0
+        _barrier(ws)
+        torch.cuda.synchronize()
+    ms = _max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps, ws)
+    value = ws * ops / (ms * 1e-3) / 1e12
+
+    # ---- dominant kernel alone: the stacked gate/up GEMM, CUDA events around it
+    gu = block.gate_up
+    with torch.inference_mode():
+        q, sx = tq.quantize_activation_tile_absmax(acts["x_gu"])
+        kw = dict(x_fp=acts["x_gu"], x_int8=q, sx=sx, out_dtype=torch.bfloat16, **gu._weights())
+        for _ in range(3):
+            tq.gemm_mixed_rows_splitk(**kw)
+        kev = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(max(5, args.steps // 4))]
+        for e0, e1 in kev:
+            flush.zero_()
+            e0.record()
+            tq.gemm_mixed_rows_splitk(**kw)
+            e1.record()
+        torch.cuda.synchronize()
+    k_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in kev)
+    k_ops = 2 * rows * gu.M_orig * gu.K_orig
+    peak, peak_src = _int8_peak(device)
+    achieved = k_ops / (k_ms * 1e-3) / 1e12
+
+    # ---- e2e: whole block through the module API, host buffers in and out
+    host_in = hidden.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    with torch.inference_mode():
+        for _ in range(2):
+            block.forward(hidden)
+        torch.cuda.synchronize()
+        e2e_steps = max(3, args.steps // 10)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(e2e_steps):
+            out = block.forward(host_in.to(device, non_blocking=True))
+            host_out.copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws)
+
+    # ---- the whole block (attention, norms included), device resident, for context
+    with torch.inference_mode():
+        bev = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(5)]
+        for e0, e1 in bev:
+            flush.zero_()
+            e0.record()
+            block.forward(hidden)
+            e1.record()
+        torch.cuda.synchronize()
+    block_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in bev)
+
+    line = {
+        "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 (exact i32 tile products) + bf16, f32 accumulate",
+        "data": "synthetic (seeded random init)",
+        "config": {"workload": "config2: Llama-3.2-3B decoder block prefill", "rows": rows, "hidden": 3072,
+                   "intermediate": 8192, "heads": "24/8", "keep_bf16": KEEP, "tile": "64x64",
+                   "parallelism": f"replicas x{ws}", "l2": "flushed (256 MB write) between timed steps"},
+        "roofline": {"kernel": "mixed GEMM, stacked gate/up (8192 x 16384 x 3072)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+                     "frac": round(achieved / peak, 3), "peak_source": peak_src, "ops_per_launch": k_ops,
+                     "launch_ms": round(k_ms, 4), "traffic": None,
+                     "frac_of_bf16_measured": round(achieved / _peaks().get("bf16_tflops", 1639.7), 3)},
+        "e2e": {"value": round(ws * ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
+                "h2d_bytes_per_step": hidden.numel() * 2, "d2h_bytes_per_step": hidden.numel() * 2,
+                "what": "whole decoder block through MixedLinear modules, pinned host in/out"},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "block_ms": round(block_ms, 4),
+    }
+    if rank == 0:
+        secs, cops = _cpu_sample(acts, block, args.cpu_rows)
+        line["cpu_baseline"] = {"value": cops / secs / 1e12, "unit": "TOPS", "cores": os.cpu_count() or 1,
+                                "kind": "port",
+                                "sample": f"{args.cpu_rows} of 8192 rows through the 4 linears "
+                                          "(oracle/tq_oracle.c restatement of the reference, OpenMP)"}
+    return line
+
+
+def run_decode(args, ws, rank, device):
+    """Config 1: one q_proj-shaped MixedLinear (3072 x 3072, 1 % BF16), 16 tokens."""
+    import tilequant_b200 as tq
+    from tests.golden import inputs as I
+    from tilequant_b200 import _native as N
+
+    x, w, fp16, int8, n_tr, n_tc = I.config1(0)
+    nrot = 40  # distinct weight copies: 40 x 9.75 MB > 2x L2
+    lins = []
+    for _ in range(nrot):
+        p = tq.pack_weight_from_tile_ids(w.to(device), n_tr=n_tr, n_tc=n_tc, int8_tile_ids=int8, fp16_tile_ids=fp16,
+                                         cfg=_cfg())
+        lins.append(tq.MixedLinear(p, None, _cfg()))
+    xd = x.to(device)
+    l0 = lins[0]
+    bytes_per = (l0.int8_tiles.numel() + l0.fp16_tiles.numel() * 2 + l0.int8_scales.numel() * 4 +
+                 (l0.int8_tile_ids.numel() + l0.fp16_tile_ids.numel()) * 4 + 2 * (n_tr + 1) * 4 + xd.numel() * 2 +
+                 16 * 3072 * 2)
+    with torch.inference_mode():
+        for lin in lins:
+            lin(xd)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        c0 = N.kernel_launches()
+        with torch.cuda.graph(g):
+            for lin in lins:
+                lin(xd)
+        per_replay = N.kernel_launches() - c0
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        with ClockSampler(device.index) as clocks:
+            e0.record()
+            for _ in range(args.steps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+        _barrier(ws)
+    us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / (args.steps * nrot), ws)
+    gbs = ws * bytes_per / (us * 1e-6) / 1e9
+    hbm = _peaks().get("hbm_gbs", 6543.1)
+    return {
+        "metric": "mixed tile GEMM GB/s: config 1 (q_proj 3072x3072, 16 tokens, 1 % BF16), quantize+GEMM",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(us * nrot / 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 + bf16", "data": "synthetic (seeded random init)",
+        "config": {"workload": "config1: one MixedLinear decode", "rows": 16, "bytes_per_call": bytes_per,
+                   "calls_per_step": nrot, "l2": "40 distinct weight copies per step (> 2x L2)",
+                   "graph": "one CUDA graph of 40 calls per step"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / ws / hbm, 3), "traffic": None, "us_per_call": round(us, 3),
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
+        "gpu_launches": per_replay * args.steps,
+        "clocks": clocks.summary(),
+    }
+
+
+def run_reference(args, ws, rank):
+    """CPU restatement of the reference (oracle/) on a bounded sample of config 2."""
+    if rank != 0:
+        return None
+    if not torch.cuda.is_available():
+        return {"impl": "reference", "unavailable": "no CUDA device to pack the workload's weights"}
+    device = torch.device("cuda", 0)
+    block, hidden, acts, rows = _prefill_setup(device)
+    for _ in range(args.warmup):
+        _cpu_sample(acts, block, args.cpu_rows)
+    secs, ops = 0.0, 0
+    for _ in range(args.steps):
+        s, o = _cpu_sample(acts, block, args.cpu_rows)
+        secs += s
+        ops += o
+    value = ops / secs / 1e12
+    threads = os.cpu_count() or 1
+    return {
+        "impl": "reference", "metric": METRIC_PREFILL, "value": value, "unit": "TOPS", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16 (CPU)",
+        "data": "synthetic (seeded random init)",
+        "config": {"workload": "config2: Llama-3.2-3B decoder block prefill",
+                   "rows_sampled_per_linear": args.cpu_rows},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port",
+                         "sample": f"{args.cpu_rows} of 8192 rows through the 4 linears per step "
+                                   "(oracle/tq_oracle.c, OpenMP)"},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")
+    args = ap.parse_args()
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        line = run_reference(args, ws, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    line = run_decode(args, ws, rank, device) if args.workload == "decode" else run_prefill(args, ws, rank, device)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -61,6 +61,10 @@ TQ_API const char* tq_last_error(void);
 /* Static name of a status code. */
 TQ_API const char* tq_status_string(int status);
 
+/* Number of kernels this library has launched in the process so far (all devices,
+ * all streams).  Lets a caller count the native launches of a region of work. */
+TQ_API int64_t tq_kernel_launches(void);
+
 /* ---------------------------------------------------------------- quantizer
  * x is (n_rows, k) of x_dtype with element strides (ld_row, ld_col).
  * sx[c] = f32(dtype(f32(absmax(x[:, 64c:64c+64])) / 127)), 1.0 for an all-zero

@@ -27,6 +27,7 @@ SIGNATURES = {
     "tq_abi_version": [],
     "tq_last_error": [],
     "tq_status_string": [_I],
+    "tq_kernel_launches": [],
     "tq_act_scales": [_P, _I, _I64, _I64, _I64, _I64, _P, _P],
     "tq_quantize_with_scales": [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _I64, _P],
     "tq_quantize_act": [_P, _I, _I64, _I64, _I64, _I64, _P, _I64, _P, _P],
@@ -69,6 +70,7 @@ def load() -> ctypes.CDLL:
                 fn.restype = _I
             lib.tq_last_error.restype = ctypes.c_char_p
             lib.tq_status_string.restype = ctypes.c_char_p
+            lib.tq_kernel_launches.restype = ctypes.c_int64
             if lib.tq_abi_version() != ABI_VERSION:
                 raise TileQuantError("libtilequant_b200.so ABI version mismatch; rebuild it")
             _lib = lib
@@ -113,3 +115,8 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
         elif t.device != dev:
             raise ValueError(f"tensors on different devices: {dev} and {t.device}")
     return dev
+
+
+def kernel_launches() -> int:
+    """Kernels this library has launched in the process so far."""
+    return int(load().tq_kernel_launches())

@@ -100,7 +100,7 @@ extern "C" int tq_calib_gi_accumulate(const void* w, const void* g, int dtype, i
     gi_kernel<TQ_DTYPE_BF16><<<blocks, 256, 0, st>>>(W, G, m, k, ldw, ldg, n_tc, tile_scores);
   else
     gi_kernel<TQ_DTYPE_F16><<<blocks, 256, 0, st>>>(W, G, m, k, ldw, ldg, n_tc, tile_scores);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }
 
@@ -118,7 +118,7 @@ extern "C" int tq_calib_iaa_channel_accumulate(const void* x, int dtype, int64_t
     iaa_channel_kernel<TQ_DTYPE_BF16><<<dim3(cb, (unsigned)splits), 256, 0, st>>>(X, rows, k, ld_row, act_sum);
   else
     iaa_channel_kernel<TQ_DTYPE_F16><<<dim3(cb, (unsigned)splits), 256, 0, st>>>(X, rows, k, ld_row, act_sum);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }
 
@@ -132,12 +132,12 @@ extern "C" int tq_calib_iaa_tile_scores(const void* w, int dtype, int64_t m, int
   const int n_tr = (int)((m + 63) / 64), n_tc = (int)((k + 63) / 64);
   cudaStream_t st = (cudaStream_t)stream;
   iaa_mean_kernel<<<(unsigned)((k + 255) / 256), 256, 0, st>>>(act_sum, k, count, mean);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   const auto W = reinterpret_cast<const uint16_t*>(w);
   if (dtype == TQ_DTYPE_BF16)
     iaa_tile_kernel<TQ_DTYPE_BF16><<<(unsigned)((int64_t)n_tr * n_tc), 256, 0, st>>>(W, m, k, ldw, n_tc, mean, tile_scores);
   else
     iaa_tile_kernel<TQ_DTYPE_F16><<<(unsigned)((int64_t)n_tr * n_tc), 256, 0, st>>>(W, m, k, ldw, n_tc, mean, tile_scores);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }

@@ -165,6 +165,15 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
     if (_e != cudaSuccess) return tq_set_cuda_error(_e);    \
   } while (0)
 
+// Check the launch just issued and count it.
+#define TQ_LAUNCHED()                                       \
+  do {                                                      \
+    cudaError_t _e = cudaGetLastError();                    \
+    if (_e != cudaSuccess) return tq_set_cuda_error(_e);    \
+    tq_count_launch();                                      \
+  } while (0)
+
 int tq_set_cuda_error(cudaError_t e);
+void tq_count_launch(int n = 1);
 int tq_set_error(int code, const char* msg);
 int tq_sm_count();

@@ -69,6 +69,8 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
   a.n_tc = n_tc;
   a.split = split_k;
   a.has_fp16 = t16 > 0;
+  a.w8_rows = t8 * 64;
+  a.w16_rows = t16 * 64;
   cudaStream_t st = (cudaStream_t)stream;
   if (algo == TQ_ALGO_UMMA || (algo == TQ_ALGO_AUTO && n_rows > 64 &&
                                tq_umma_supported(n_rows, m, k, x_i8, ld_x8, x_fp, ld_xfp, int8_tiles, fp16_tiles))) {
@@ -139,6 +141,7 @@ extern "C" int tq_gemm_int8_partials(const int8_t* x_i8, int64_t ld_x8, const in
   a.ids8 = int8_tile_ids;
   a.rp8 = int8_row_ptr;
   a.partials = partials;
+  a.w8_rows = t8 * 64;
   a.n_rows = (int)n_rows;
   a.M = n_tr * 64;
   a.K = (int)k;

@@ -27,6 +27,8 @@ struct RowsArgs {
   int n_rows, M, K, n_tc, split;
   int n_tr;            // row tiles of the weight
   int rows_per_cta;    // row tiles one CTA streams (rows kernel, split 1)
+  int64_t w8_rows;     // 64 * T8 (rows of the INT8 arena)
+  int64_t w16_rows;    // 64 * T16
   int has_fp16;
   int a8_vec;          // x_i8 rows are 16-byte addressable
   int afp_vec;         // x_fp rows are 16-byte addressable

@@ -484,6 +484,7 @@ static int launch_rows(RowsArgs& a, const RowsMaps& maps, int n_blocks, cudaStre
   cfg.attrs = attr;
   cfg.numAttrs = na;
   TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, rows_kernel<NB, XT>, a, maps));
+  tq_count_launch();
   return TQ_OK;
 }
 

@@ -156,7 +156,7 @@ extern "C" int tq_pack_int8_tiles(const void* w, int w_dtype, int64_t m, int64_t
     pack_int8_kernel<TQ_DTYPE_BF16><<<(unsigned)t8, 256, 0, st>>>(w, m, k, ldw, n_tc, ids, col_importance, tiles, scales);
   else
     pack_int8_kernel<TQ_DTYPE_F16><<<(unsigned)t8, 256, 0, st>>>(w, m, k, ldw, n_tc, ids, col_importance, tiles, scales);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }
 
@@ -169,6 +169,6 @@ extern "C" int tq_gather_fp_tiles(const void* w, int w_dtype, int64_t m, int64_t
   if (!ids || !tiles) return tq_set_error(TQ_ERR_INVALID, "null output or id array");
   gather_fp_kernel<<<(unsigned)t16, 256, 0, (cudaStream_t)stream>>>(reinterpret_cast<const uint16_t*>(w), m, k, ldw,
                                                                     n_tc, ids, reinterpret_cast<uint16_t*>(tiles));
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }

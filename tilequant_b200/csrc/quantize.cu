@@ -218,7 +218,7 @@ static int launch_scales(const void* x, int dtype, int64_t n_rows, int64_t k, in
       act_scales_kernel<TQ_DTYPE_BF16, false><<<dim3(n_tc, 1), 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, sx, vec);
     else
       act_scales_kernel<TQ_DTYPE_F16, false><<<dim3(n_tc, 1), 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, sx, vec);
-    TQ_CUDA_TRY(cudaGetLastError());
+    TQ_LAUNCHED();
     return TQ_OK;
   }
   cudaLaunchConfig_t cfg = {};
@@ -236,6 +236,7 @@ static int launch_scales(const void* x, int dtype, int64_t n_rows, int64_t k, in
     TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_scales_kernel<TQ_DTYPE_BF16, true>, x, n_rows, k, ld_row, ld_col, sx, vec));
   else
     TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, act_scales_kernel<TQ_DTYPE_F16, true>, x, n_rows, k, ld_row, ld_col, sx, vec));
+  tq_count_launch();
   return TQ_OK;
 }
 
@@ -249,7 +250,7 @@ static int launch_quantize(const void* x, int dtype, int64_t n_rows, int64_t k, 
     quantize_kernel<TQ_DTYPE_BF16><<<(unsigned)blocks, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, sx, q, ldq, vec);
   else
     quantize_kernel<TQ_DTYPE_F16><<<(unsigned)blocks, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, sx, q, ldq, vec);
-  TQ_CUDA_TRY(cudaGetLastError());
+  TQ_LAUNCHED();
   return TQ_OK;
 }
 
@@ -286,7 +287,7 @@ extern "C" int tq_quantize_act(const void* x, int x_dtype, int64_t n_rows, int64
       quantize_small_kernel<TQ_DTYPE_BF16><<<n_tc, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, q, ldq, sx);
     else
       quantize_small_kernel<TQ_DTYPE_F16><<<n_tc, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, q, ldq, sx);
-    TQ_CUDA_TRY(cudaGetLastError());
+    TQ_LAUNCHED();
     return TQ_OK;
   }
   rc = launch_scales(x, x_dtype, n_rows, k, ld_row, ld_col, sx, st);

@@ -29,6 +29,14 @@ int tq_sm_count() {
   return cached[dev];
 }
 
+#include <atomic>
+
+static std::atomic<int64_t> g_launches{0};
+
+void tq_count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+extern "C" int64_t tq_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
 extern "C" int tq_abi_version(void) { return 1; }
 
 extern "C" const char* tq_last_error(void) { return g_last_error; }
