@@ -59,3 +59,19 @@ def assert_close_with_bias(y_bits, ref_bits, bias_bits, what: str = "", dtype_co
     tol = ulp_bf16(r - b) + ulp_bf16(r)
     bad = np.abs(y - r) > tol
     assert not bad.any(), f"{what}: {int(bad.sum())} elements beyond one pre-bias ulp"
+
+
+def assert_close_gemm(y_bits, ref_bits, what: str = "", rms_frac: float = 1e-3, dtype_code: int = 0):
+    """GEMM outputs whose 16-bit tile dots were summed in another order: within one
+    BF16 ulp of the reference, except near zero where cancellation makes ulps tiny;
+    there the difference must stay below rms_frac of the output's RMS magnitude."""
+    y = f16bits_to_f32(y_bits, dtype_code).astype(np.float64)
+    r = f16bits_to_f32(ref_bits, dtype_code).astype(np.float64)
+    rms = float(np.sqrt(np.mean(r * r))) if r.size else 0.0
+    tol = np.maximum(ulp_bf16(r), rms_frac * rms)
+    bad = np.abs(y - r) > tol
+    if bad.any():
+        idx = np.argwhere(bad)[:5]
+        detail = ", ".join(f"{tuple(i)}: got {y[tuple(i)]:.6g} ref {r[tuple(i)]:.6g}" for i in idx)
+        raise AssertionError(f"{what}: {int(bad.sum())} elements beyond tolerance (rms {rms:.4g}): {detail}")
+    return np.abs(y - r)

@@ -167,7 +167,7 @@ def _gemm_case(name):
     return x, p, M, K, int(GEMM[f"{name}__split"][0]), bias
 
 
-def _run_gemm(x_bits, p, M, K, split, bias_bits, fused=False):
+def _run_gemm(x_bits, p, M, K, split, bias_bits, fused=False, algo=0):
     x = to_torch16(x_bits, torch.bfloat16, DEV)
     bias = None if bias_bits is None else to_torch16(bias_bits, torch.bfloat16, DEV)
     kw = dict(int8_tiles=p.int8_tiles, int8_scales=p.int8_scales, int8_tile_ids=p.int8_tile_ids,
@@ -177,7 +177,7 @@ def _run_gemm(x_bits, p, M, K, split, bias_bits, fused=False):
     if fused:
         return tq.gemm_mixed_fused_quant(x_fp=x, **kw)
     q, sx = tq.quantize_activation_tile_absmax(x)
-    return tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, **kw)
+    return tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, algo=algo, **kw)
 
 
 @pytest.mark.parametrize("name", _cases(GEMM, "__y"))
@@ -207,12 +207,13 @@ def _int8_only_pack(w, n_tr, n_tc):
 @pytest.mark.parametrize("rows,m,k,split", [(1, 64, 64, 1), (16, 3072, 3072, 8), (7, 200, 136, 3), (33, 512, 1024, 16),
                                             (64, 1024, 3072, 4), (130, 256, 512, 2), (300, 192, 320, 1)])
 def test_gemm_int8_only_bit_exact_vs_oracle(cuda_device, rows, m, k, split):
-    """Without 16-bit tiles the reference arithmetic is fully specified: exact."""
+    """Without 16-bit tiles the reference arithmetic is fully specified: the split-K
+    row kernel (mul then add, as the reference source reads) is bit-exact."""
     x = I.activations(rows, k, 200 + rows, outliers=2)
     w = I.weight(m, k, 201 + m)
     n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
     p = _int8_only_pack(w, n_tr, n_tc)
-    y = from_torch16(_run_gemm(I.bits(x), p, m, k, split, None))
+    y = from_torch16(_run_gemm(I.bits(x), p, m, k, split, None, algo=1))
     q, sx = O.quantize_act(I.bits(x))
     pk = O.pack(I.bits(w), n_tr, n_tc, np.arange(n_tr * n_tc), np.arange(0))
     ref = O.gemm(q, sx, pk, I.bits(x), m, k, split_k=split, use_fma=False)

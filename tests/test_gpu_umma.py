@@ -17,7 +17,7 @@ import torch
 import tilequant_b200 as tq
 from oracle import oracle as O
 from tests.golden import inputs as I
-from tests.helpers import assert_close_with_bias, assert_within_ulp, from_torch16
+from tests.helpers import assert_close_gemm, assert_close_with_bias, from_torch16, ulp_dist16
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -67,8 +67,8 @@ def test_umma_mixed_within_one_ulp(cuda_device, rows, m, k, keep):
     y = from_torch16(_run(x, p, m, k))
     q, sx = O.quantize_act(I.bits(x))
     ref = O.gemm(q, sx, pk, I.bits(x), m, k, split_k=1, use_fma=True)
-    d = assert_within_ulp(y, ref, 1, f"rows={rows}")
-    assert (d == 0).mean() > 0.98
+    assert_close_gemm(y, ref, f"rows={rows}")
+    assert (ulp_dist16(y, ref) == 0).mean() > 0.98
 
 
 def test_umma_partials_bit_exact(cuda_device):

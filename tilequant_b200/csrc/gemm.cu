@@ -72,7 +72,7 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
   a.w8_rows = t8 * 64;
   a.w16_rows = t16 * 64;
   cudaStream_t st = (cudaStream_t)stream;
-  if (algo == TQ_ALGO_UMMA || (algo == TQ_ALGO_AUTO && n_rows > 64 &&
+  if (algo == TQ_ALGO_UMMA || (algo == TQ_ALGO_AUTO && n_rows > 64 && t8 > 0 &&
                                tq_umma_supported(n_rows, m, k, x_i8, ld_x8, x_fp, ld_xfp, int8_tiles, fp16_tiles))) {
     if (!tq_umma_supported(n_rows, m, k, x_i8, ld_x8, x_fp, ld_xfp, int8_tiles, fp16_tiles))
       return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: unsupported shape or alignment");
