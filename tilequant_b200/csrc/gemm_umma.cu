@@ -14,12 +14,13 @@
 // row tile whose tile at that column is 16-bit, or that does not exist, is loaded as an
 // out-of-bounds TMA box, i.e. zeros, and its step is skipped in the rescale, so each row
 // tile still sees exactly its own INT8 tiles in ascending order).  The 16-bit tiles of
-// each row tile then run as N = 64 kind::f16 MMAs into an FP32 TMEM accumulator.
+// each row tile then run as N = 64 kind::f16 MMAs into an FP32 TMEM accumulator, as one
+// more step of the same TMEM ring.
 //
 // Warp roles (one CTA per SM, persistent over output tiles, 11 warps):
-//   warp 0      TMA producer (one thread): 10-stage shared-memory ring, 16 KB per stage,
-//               SWIZZLE_64B (the UMMA canonical K-major layout);
-//   warp 1      MMA issuer (one thread); tcgen05.commit frees stages and publishes tiles;
+//   warp 0      TMA producer (one thread): 6-stage shared-memory ring, each stage two K
+//               steps (2 x 16 KB), SWIZZLE_64B (the UMMA canonical K-major layout);
+//   warp 1      MMA issuer (one thread); tcgen05.commit frees stages and publishes groups;
 //   warp 2      scheduler: builds each output tile's column table (INT8 list position
 //               and combined scale sx*sw of both row tiles at every column, 16-bit tile
 //               columns) one tile ahead into a 2-slot ring, so no role stalls on the
@@ -30,8 +31,12 @@
 //               dot (exact: |dot| <= 64*128*128 < 2^22); a packed f32x2 add recovers the
 //               dot, a packed f32x2 FMA rescales it into the FP32 accumulator held in
 //               registers; the preset is rewritten after every read.
-// TMEM (512 columns): [0,128) and [128,256) INT32 tiles (double buffer), [256,384) FP32
-// 16-bit sums of the two row tiles.
+// TMEM (512 columns): two groups of two 128-column step buffers.  Every barrier hand-off
+// (stage full / empty, group full / empty) covers two K steps: an mbarrier round trip
+// and the tcgen05 fences around it cost about as much as one step's MMA, so per-step
+// hand-offs left the tensor pipe idle most of the time.
+// The FP32 rescale (one add + one FMA per output element and K step: 256 FP32-pipe
+// cycles per step and SM, twice the step's MMA time) is the bound of this kernel.
 #include <string.h>
 
 #include <algorithm>
@@ -44,13 +49,19 @@ namespace tq {
 
 namespace um {
 constexpr int BM = 128;             // activation rows per output tile (MMA M)
-constexpr int NS = 10;              // shared-memory stages
-constexpr int A_BYTES = BM * 64;    // 8 KB activation tile
+constexpr int A_BYTES = BM * 64;    // 8 KB activation tile of one K step
 constexpr int W_BYTES = 64 * 64;    // 4 KB weight tile
-constexpr int STAGE = A_BYTES + 2 * W_BYTES;
-constexpr int THREADS = 352;        // 11 warps
+constexpr int STEP_BYTES = A_BYTES + 2 * W_BYTES;
+constexpr int GS = 2;               // K steps per pipeline stage and per TMEM group
+constexpr int STAGE = GS * STEP_BYTES;
+constexpr int NS = 6;               // shared-memory stages
 constexpr int EPI_WARP0 = 3;
+constexpr int NEPI = 8;             // epilogue warps: 4 lane quadrants x (NEPI / 4) column slices
+constexpr int CW = 128 / (NEPI / 4);  // columns of a step one epilogue warp rescales
+constexpr int THREADS = (EPI_WARP0 + NEPI) * 32;
+constexpr int NG = 2;               // TMEM groups of GS 128-column step buffers
 constexpr int TMEM_COLS = 512;
+static_assert(NG * GS * 128 <= TMEM_COLS, "TMEM ring does not fit");
 constexpr uint32_t MAGIC = 0x4B400000u;  // bits of 2^23 + 2^22
 constexpr float MAGIC_F = 12582912.0f;
 
@@ -103,6 +114,18 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// 32 consecutive TMEM columns of this thread's lane (no wait).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // 16 consecutive TMEM columns of this thread's lane (no wait).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
   asm volatile(
@@ -111,16 +134,67 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
         "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for this thread's TMEM loads; the 16 destination registers of the last load are
+// operands so no use of them can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait_ld_regs16(uint32_t* v) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
+// Wait for this thread's TMEM loads, with the 32 destination registers of the last load
+// as operands so no use of them can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t* v) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                 "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]),
+                 "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]),
+                 "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]),
+                 "+r"(v[30]), "+r"(v[31])
+               :
+               : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// The same 32-bit value into 32 consecutive TMEM columns of this thread's lane (no wait).
+// The same 32-bit value into 32 consecutive TMEM columns of this thread's lane (no wait),
+// as four 8-column stores: the store's source is a register vector, and eight copies of
+// the value keep the register footprint small next to the live accumulator.
 __device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t x) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-      "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-      "r"(x)
-      : "memory");
+#pragma unroll
+  for (int u = 0; u < 32; u += 8)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr + u), "r"(x)
+                 : "memory");
+}
+
+// The 8-register source vector `m` (every element the same value) into 16 consecutive TMEM
+// columns of this thread's lane (no wait).  The caller keeps `m` in registers for the
+// whole loop: a store's source must be a register vector, and rebuilding eight copies of
+// a constant before every store costs as many instructions as the rescale itself.
+__device__ __forceinline__ void tmem_fill16(uint32_t taddr, const uint32_t (&m)[8]) {
+#pragma unroll
+  for (int u = 0; u < 16; u += 8)
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr + u), "r"(m[0]),
+                 "r"(m[1]), "r"(m[2]), "r"(m[3]), "r"(m[4]), "r"(m[5]), "r"(m[6]), "r"(m[7])
+                 : "memory");
+}
+
+// acc[e] = fma(dot, s, acc[e]) for 16 columns whose TMEM words hold 2^23 + 2^22 + dot;
+// with DUMP, also writes the INT32 dots of an INT8 tile (p >= 0) to `partials`.
+template <bool DUMP>
+__device__ __forceinline__ void rescale16(float2* acc, const uint32_t* v, float s, int32_t* partials, int p, int row,
+                                          int n_rows, int col) {
+  const float2 s2 = make_float2(s, s), neg_magic = make_float2(-um::MAGIC_F, -um::MAGIC_F);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float2 m = make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+    acc[e] = __ffma2_rn(__fadd2_rn(m, neg_magic), s2, acc[e]);  // the add is exact: the tile dot
+  }
+  if (DUMP && p >= 0 && row < n_rows) {
+    int32_t* base = partials + ((int64_t)p * n_rows + row) * 64 + col;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) base[e] = (int32_t)(v[e] - um::MAGIC);
+  }
 }
 
 struct TileHdr {
@@ -129,20 +203,18 @@ struct TileHdr {
   int b16[2];         // first 16-bit list position of each row tile
 };
 
-template <int XT>
+template <int XT, bool DUMP>
 __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, const __grid_constant__ UmmaMaps maps) {
   using namespace um;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int n_tc = a.n_tc;
-  uint8_t* stages = smem;  // NS x (A 8 KB | W0 4 KB | W1 4 KB), 1024-byte aligned
+  uint8_t* stages = smem;  // NS x GS x (A 8 KB | W0 4 KB | W1 4 KB), 1024-byte aligned
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * STAGE);
   uint64_t* sempty = full + NS;
-  uint64_t* tfull = sempty + NS;   // [2]
-  uint64_t* tempty = tfull + 2;    // [2]
-  uint64_t* bfull = tempty + 2;
-  uint64_t* bempty = bfull + 1;
-  uint64_t* qfull = bempty + 1;    // [2] column table ready
+  uint64_t* tfull = sempty + NS;   // [NG] TMEM group written by the MMA
+  uint64_t* tempty = tfull + NG;   // [NG] TMEM group read and preset again
+  uint64_t* qfull = tempty + NG;   // [2] column table ready
   uint64_t* qempty = qfull + 2;    // [2] column table consumed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qempty + 2);
   uint8_t* tables = smem + NS * STAGE + 512;
@@ -163,14 +235,14 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
       mbar_init(&full[i], 1);
       mbar_init(&sempty[i], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NG; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);
-      mbar_init(&qfull[b], 32);
-      mbar_init(&qempty[b], 3);
+      mbar_init(&tempty[b], NEPI);
     }
-    mbar_init(bfull, 1);
-    mbar_init(bempty, 8);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qfull[s], 32);
+      mbar_init(&qempty[s], 3);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -248,28 +320,35 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
         const int slot = k & 1;
         if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
-        const TileHdr h = *t_hdr(slot);
+        const TileHdr* h = t_hdr(slot);
+        const int tb = h->tb, n_r = h->n_r;
         const int* pos = t_pos(slot);
         const int* bcol = t_bcol(slot);
-        for (int c = 0; c < n_tc; ++c, ++g) {
-          const int stg = g % NS;
+        for (int c0 = 0; c0 < n_tc; c0 += GS, ++g) {  // GS INT8 K steps per stage
+          const int stg = g % NS, ns = min(GS, n_tc - c0);
           if (ok && !mbar_wait_bounded(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
-          uint8_t* sa = stages + stg * STAGE;
-          mbar_expect_tx(&full[stg], STAGE);
-          tma_load_2d(sa, &maps.x8, c * 64, h.tb * BM, &full[stg]);
-          const int p0 = pos[c], p1 = pos[n_tc + c];
-          tma_load_2d(sa + A_BYTES, &maps.w8, 0, p0 >= 0 ? p0 * 64 : oob_row, &full[stg]);
-          tma_load_2d(sa + A_BYTES + W_BYTES, &maps.w8, 0, p1 >= 0 ? p1 * 64 : oob_row, &full[stg]);
+          mbar_expect_tx(&full[stg], ns * STEP_BYTES);
+          for (int s = 0; s < ns; ++s) {
+            const int c = c0 + s;
+            uint8_t* sa = stages + stg * STAGE + s * STEP_BYTES;
+            tma_load_2d(sa, &maps.x8, c * 64, tb * BM, &full[stg]);
+            const int p0 = pos[c], p1 = pos[n_tc + c];
+            tma_load_2d(sa + A_BYTES, &maps.w8, 0, p0 >= 0 ? p0 * 64 : oob_row, &full[stg]);
+            tma_load_2d(sa + A_BYTES + W_BYTES, &maps.w8, 0, p1 >= 0 ? p1 * 64 : oob_row, &full[stg]);
+          }
         }
-        for (int j = 0; j < h.n_r; ++j) {
-          for (int i = 0; i < 2 * h.n16[j]; ++i, ++g) {
+        for (int j = 0; j < n_r; ++j) {  // one 16-bit tile (two 32-column halves) per stage
+          const int n16 = h->n16[j], b16 = h->b16[j];
+          for (int i = 0; i < n16; ++i, ++g) {
             const int stg = g % NS;
             if (ok && !mbar_wait_bounded(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
-            uint8_t* sa = stages + stg * STAGE;
-            const int c = bcol[j * n_tc + (i >> 1)], half = i & 1;
-            mbar_expect_tx(&full[stg], A_BYTES + W_BYTES);
-            tma_load_2d(sa, &maps.xfp, c * 64 + half * 32, h.tb * BM, &full[stg]);
-            tma_load_2d(sa + A_BYTES, &maps.w16, half * 32, (h.b16[j] + (i >> 1)) * 64, &full[stg]);
+            const int c = bcol[j * n_tc + i];
+            mbar_expect_tx(&full[stg], 2 * (A_BYTES + W_BYTES));
+            for (int half = 0; half < 2; ++half) {
+              uint8_t* sa = stages + stg * STAGE + half * STEP_BYTES;
+              tma_load_2d(sa, &maps.xfp, c * 64 + half * 32, tb * BM, &full[stg]);
+              tma_load_2d(sa + A_BYTES, &maps.w16, half * 32, (b16 + i) * 64, &full[stg]);
+            }
           }
         }
         mbar_arrive(&qempty[slot]);
@@ -278,143 +357,155 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
   } else if (warp == 1) {
     // ================================================================ MMA issuer
     if (lane == 0) {
-      uint32_t g = 0, k = 0, k8 = 0, nbf = 0;
+      uint32_t g = 0, k = 0, grp = 0;
       const uint32_t idesc16 = XT == TQ_DTYPE_BF16 ? IDESC_BF16 : IDESC_F16;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
         const int slot = k & 1;
         if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
-        const TileHdr h = *t_hdr(slot);
+        const TileHdr* h = t_hdr(slot);
+        const int n_r = h->n_r, n16_0 = h->n16[0], n16_1 = h->n16[1];
         mbar_arrive(&qempty[slot]);  // only the header was needed
-        for (int c = 0; c < n_tc; ++c, ++g, ++k8) {
-          const int stg = g % NS;
-          const uint32_t b = k8 & 1;
+        for (int c0 = 0; c0 < n_tc; c0 += GS, ++g, ++grp) {
+          const int stg = g % NS, ns = min(GS, n_tc - c0);
+          const uint32_t gb = grp % NG;
           if (ok && !mbar_wait_bounded(&full[stg], (g / NS) & 1, a.err)) ok = false;
-          if (ok && !mbar_wait_bounded(&tempty[b], (k8 >> 1) & 1, a.err)) ok = false;
+          if (ok && !mbar_wait_bounded(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
           tc_fence_after();
-          const uint32_t sa = smem_u32(stages + stg * STAGE);
-          const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
-          // the TMEM tile holds the preset; both K halves accumulate onto it
-          umma(tmem + b * 128, da, db, IDESC_I8, 1, true);
-          umma(tmem + b * 128, da + 2, db + 2, IDESC_I8, 1, true);
+          for (int s = 0; s < ns; ++s) {
+            const uint32_t sa = smem_u32(stages + stg * STAGE + s * STEP_BYTES);
+            const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
+            const uint32_t d = tmem + (gb * GS + s) * 128;
+            // the step buffer holds the preset; both K halves accumulate onto it
+            umma(d, da, db, IDESC_I8, 1, true);
+            umma(d, da + 2, db + 2, IDESC_I8, 1, true);
+          }
           umma_commit(&sempty[stg]);
-          umma_commit(&tfull[b]);
+          umma_commit(&tfull[gb]);
         }
-        const int nb = 2 * (h.n16[0] + h.n16[1]);
-        if (nb > 0) {
-          if (ok && !mbar_wait_bounded(bempty, nbf & 1, a.err)) ok = false;
+        if (n16_0 + n16_1 > 0) {  // the 16-bit tiles: one more group, first buffer only
+          const uint32_t gb = grp % NG;
+          if (ok && !mbar_wait_bounded(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
           tc_fence_after();
-          for (int j = 0; j < h.n_r; ++j) {
-            for (int i = 0; i < 2 * h.n16[j]; ++i, ++g) {
+          for (int j = 0; j < n_r; ++j) {
+            const int n16 = j == 0 ? n16_0 : n16_1;
+            for (int i = 0; i < n16; ++i, ++g) {
               const int stg = g % NS;
               if (ok && !mbar_wait_bounded(&full[stg], (g / NS) & 1, a.err)) ok = false;
               tc_fence_after();
-              const uint32_t sa = smem_u32(stages + stg * STAGE);
-              const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
-              umma(tmem + 256 + j * 64, da, db, idesc16, i == 0 ? 0 : 1, false);
-              umma(tmem + 256 + j * 64, da + 2, db + 2, idesc16, 1, false);
+              for (int half = 0; half < 2; ++half) {
+                const uint32_t sa = smem_u32(stages + stg * STAGE + half * STEP_BYTES);
+                const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
+                const uint32_t d = tmem + gb * GS * 128 + j * 64;
+                // the first MMA of a row tile overwrites the preset
+                umma(d, da, db, idesc16, (i == 0 && half == 0) ? 0 : 1, false);
+                umma(d, da + 2, db + 2, idesc16, 1, false);
+              }
               umma_commit(&sempty[stg]);
             }
           }
-          umma_commit(bfull);
-          ++nbf;
+          umma_commit(&tfull[gb]);
+          ++grp;
         }
       }
     }
   } else {
     // ================================================================ epilogue
-    const int ew = warp - EPI_WARP0;  // 0..7
+    const int ew = warp - EPI_WARP0;
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
-    const int j = ew >> 2;            // row tile of the pair: columns [64j, 64j+64)
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    // preset both INT32 tiles, then hand them (and the FP32 sums) to the MMA issuer
-    for (int b = 0; b < 2; ++b) {
-      tmem_fill32(tmem + lane_base + b * 128 + j * 64, MAGIC);
-      tmem_fill32(tmem + lane_base + b * 128 + j * 64 + 32, MAGIC);
-    }
+    const int cs = ew >> 2;           // CW-column slice of the 128-column step
+    const uint32_t col = cs * CW;
+    const int j = col >> 6;           // row tile of the pair
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + col;
+    // preset this slice of every step buffer, then hand the groups to the MMA issuer
+    for (int b = 0; b < NG * GS; ++b)
+      for (int u = 0; u < CW; u += 32) tmem_fill32(tbase + b * 128 + u, MAGIC);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&tempty[0]);
-      mbar_arrive(&tempty[1]);
-      mbar_arrive(bempty);
-    }
-    uint32_t k = 0, k8 = 0, nbf = 0;
-    const float2 neg_magic = make_float2(-MAGIC_F, -MAGIC_F);
+    if (lane == 0)
+      for (int b = 0; b < NG; ++b) mbar_arrive(&tempty[b]);
+    uint32_t k = 0, grp = 0;
+    uint32_t magic8[8];  // the preset as a store source vector, pinned in registers
+#pragma unroll
+    for (int e = 0; e < 8; ++e) magic8[e] = MAGIC;
+    asm volatile("" : "+r"(magic8[0]), "+r"(magic8[1]), "+r"(magic8[2]), "+r"(magic8[3]), "+r"(magic8[4]),
+                 "+r"(magic8[5]), "+r"(magic8[6]), "+r"(magic8[7]));
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
       const int slot = k & 1;
       if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
-      const TileHdr h = *t_hdr(slot);
+      const TileHdr* h = t_hdr(slot);
       const float* scl = t_scl(slot) + j * n_tc;
       const int* pos = t_pos(slot) + j * n_tc;
-      const int row = h.tb * BM + q * 32 + lane;  // this thread's activation row
-      float2 acc[32];
+      const int row = h->tb * BM + q * 32 + lane;  // this thread's activation row
+      float2 acc[CW / 2];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) acc[e] = make_float2(0.0f, 0.0f);
-      for (int c = 0; c < n_tc; ++c, ++k8) {
-        const uint32_t b = k8 & 1;
-        if (ok && !mbar_wait_bounded(&tfull[b], (k8 >> 1) & 1, a.err)) ok = false;
+      for (int e = 0; e < CW / 2; ++e) acc[e] = make_float2(0.0f, 0.0f);
+      static_assert(GS == 2 && CW % 16 == 0, "the rescale pipeline below is written for 2-step groups");
+      for (int c0 = 0; c0 < n_tc; c0 += GS, ++grp) {
+        const uint32_t gb = grp % NG;
+        const bool two = c0 + 1 < n_tc;
+        // A step whose tile at this column is 16-bit or missing was an MMA with a zero
+        // box: its buffer still reads 2^23 + 2^22 (dot 0), and with scale 0 the FMA
+        // leaves the accumulator bit-identical (it is never -0), so every step of the
+        // group runs the same branch-free sequence.
+        const float sc0 = scl[c0], sc1 = two ? scl[c0 + 1] : 0.0f;
+        const int p0 = pos[c0], p1 = two ? pos[c0 + 1] : -1;
+        const uint32_t t0 = tbase + gb * GS * 128;  // step s, half u at t0 + s * 128 + u * 32
+        if (ok && !mbar_wait_bounded(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
         tc_fence_after();
-        const uint32_t taddr = tmem + lane_base + b * 128 + j * 64;
-        uint32_t v[64];
-        tmem_ld16(taddr, v);
-        tmem_ld16(taddr + 16, v + 16);
-        tmem_ld16(taddr + 32, v + 32);
-        tmem_ld16(taddr + 48, v + 48);
-        tmem_wait_ld();
-        tmem_fill32(taddr, MAGIC);
-        tmem_fill32(taddr + 32, MAGIC);
-        const float s = scl[c];
-        if (pos[c] >= 0) {  // this row tile's tile at column c is INT8
-          const float2 s2 = make_float2(s, s);
+        // 16-column chunks (step s = i / CPS, columns 16 * (i % CPS)), each chunk's load
+        // issued before the previous chunk's rescale so the TMEM latency overlaps FP work
+        constexpr int CPS = CW / 16;  // chunks per step
+        uint32_t v[2][16];
+        tmem_ld16(t0, v[0]);
+        tmem_wait_ld_regs16(v[0]);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float2 m = make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
-            acc[e] = __ffma2_rn(__fadd2_rn(m, neg_magic), s2, acc[e]);  // the add is exact: the tile dot
-          }
-          if (a.partials && row < a.n_rows) {
-            int32_t* base = a.partials + ((int64_t)pos[c] * a.n_rows + row) * 64;
-#pragma unroll
-            for (int e = 0; e < 64; ++e) base[e] = (int32_t)(v[e] - MAGIC);
-          }
+        for (int i = 0; i < GS * CPS; ++i) {
+          const uint32_t ti = t0 + (i / CPS) * 128 + (i % CPS) * 16;
+          if (i + 1 < GS * CPS) tmem_ld16(t0 + ((i + 1) / CPS) * 128 + ((i + 1) % CPS) * 16, v[(i + 1) & 1]);
+          tmem_fill16(ti, magic8);
+          rescale16<DUMP>(acc + (i % CPS) * 8, v[i & 1], (i / CPS) ? sc1 : sc0, a.partials, (i / CPS) ? p1 : p0, row,
+                          a.n_rows, (col & 63) + (i % CPS) * 16);
+          if (i + 1 < GS * CPS) tmem_wait_ld_regs16(v[(i + 1) & 1]);
         }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
+        if (lane == 0) mbar_arrive(&tempty[gb]);
       }
-      const int nb = 2 * (h.n16[0] + h.n16[1]);
-      if (nb > 0) {
-        if (ok && !mbar_wait_bounded(bfull, nbf & 1, a.err)) ok = false;
-        tc_fence_after();
-        if (j < h.n_r && h.n16[j] > 0) {
-          uint32_t v[64];
-          const uint32_t taddr = tmem + lane_base + 256 + j * 64;
-          tmem_ld16(taddr, v);
-          tmem_ld16(taddr + 16, v + 16);
-          tmem_ld16(taddr + 32, v + 32);
-          tmem_ld16(taddr + 48, v + 48);
+      if (h->n16[0] + h->n16[1] > 0) {
+        const uint32_t gb = grp % NG;
+        if (ok && !mbar_wait_bounded(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
+        if (j < h->n_r && h->n16[j] > 0) {  // (a row tile without 16-bit tiles kept the preset)
+          tc_fence_after();
+          const uint32_t taddr = tbase + gb * GS * 128;
+          uint32_t v[CW];
+#pragma unroll
+          for (int u = 0; u < CW; u += 32) tmem_ld32(taddr + u, v + u);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
+          for (int u = 0; u < CW; u += 32) tmem_fill32(taddr + u, MAGIC);
+#pragma unroll
+          for (int e = 0; e < CW / 2; ++e)
             acc[e] = __fadd2_rn(acc[e], make_float2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])));
+          tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bempty);
-        ++nbf;
+        if (lane == 0) mbar_arrive(&tempty[gb]);
+        ++grp;
       }
-      named_bar_sync(1, 256);  // all epilogue threads are done with this table slot
+      const int r = h->r0 + j, n_r = h->n_r;
+      named_bar_sync(1, NEPI * 32);  // all epilogue threads are done with this table slot
       if (tid == EPI_WARP0 * 32) mbar_arrive(&qempty[slot]);
-      const int r = h.r0 + j;
-      if (j < h.n_r && row < a.n_rows && a.out) {
-        const int col0 = r * 64;
+      if (j < n_r && row < a.n_rows && a.out) {
+        const int col0 = r * 64 + (col & 63);
         const int ot = a.out_dtype;
         uint16_t* orow = reinterpret_cast<uint16_t*>(a.out) + (int64_t)row * a.ldo + col0;
         const uint16_t* brow = a.bias ? reinterpret_cast<const uint16_t*>(a.bias) + col0 : nullptr;
-        const bool vec = col0 + 64 <= a.M && (((uintptr_t)orow) & 15) == 0;
+        const bool vec = col0 + CW <= a.M && (((uintptr_t)orow) & 15) == 0;
 #pragma unroll
-        for (int part = 0; part < 4; ++part) {
+        for (int part = 0; part < CW / 16; ++part) {
           uint32_t packed[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -446,13 +537,13 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
   }
 }
 
-template <int XT>
+template <int XT, bool DUMP>
 static int launch_umma_t(const RowsArgs& a, const UmmaMaps& maps, cudaStream_t st) {
   static uint64_t configured = 0;
   int dev = 0;
   TQ_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && !(configured & (1ull << dev))) {
-    TQ_CUDA_TRY(cudaFuncSetAttribute(umma_kernel<XT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    TQ_CUDA_TRY(cudaFuncSetAttribute(umma_kernel<XT, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     configured |= 1ull << dev;
   }
   // more than half the SM's shared memory: one CTA (and its 512 TMEM columns) per SM
@@ -474,7 +565,7 @@ static int launch_umma_t(const RowsArgs& a, const UmmaMaps& maps, cudaStream_t s
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, umma_kernel<XT>, a, maps));
+  TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, umma_kernel<XT, DUMP>, a, maps));
   tq_count_launch();
   return TQ_OK;
 }
@@ -515,5 +606,7 @@ int tq_launch_umma(const RowsArgs& a_in, int n_tr, int fp_dtype, cudaStream_t st
   if (a.has_fp16 && tq_encode_2d(&maps.w16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, a.w16, 64, (uint64_t)a.w16_rows, 128,
                                  32, 64, CU_TENSOR_MAP_SWIZZLE_64B) != TQ_OK)
     return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: 16-bit tile tensor map");
-  return fp_dtype == TQ_DTYPE_BF16 ? launch_umma_t<TQ_DTYPE_BF16>(a, maps, st) : launch_umma_t<TQ_DTYPE_F16>(a, maps, st);
+  if (a.partials) return launch_umma_t<TQ_DTYPE_BF16, true>(a, maps, st);  // INT8 only: no 16-bit tiles
+  return fp_dtype == TQ_DTYPE_BF16 ? launch_umma_t<TQ_DTYPE_BF16, false>(a, maps, st)
+                                   : launch_umma_t<TQ_DTYPE_F16, false>(a, maps, st);
 }
