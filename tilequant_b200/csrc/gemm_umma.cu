@@ -17,7 +17,7 @@
 // each row tile then run as N = 64 kind::f16 MMAs into an FP32 TMEM accumulator, as one
 // more step of the same TMEM ring.
 //
-// Warp roles (one CTA per SM, persistent over output tiles, 11 warps):
+// Warp roles (one CTA per SM, persistent over output tiles, 12 warps):
 //   warp 0      TMA producer (one thread): 6-stage shared-memory ring, each stage two K
 //               steps (2 x 16 KB), SWIZZLE_64B (the UMMA canonical K-major layout);
 //   warp 1      MMA issuer (one thread); tcgen05.commit frees stages and publishes groups;
@@ -25,7 +25,8 @@
 //               and combined scale sx*sw of both row tiles at every column, 16-bit tile
 //               columns) one tile ahead into a 2-slot ring, so no role stalls on the
 //               id lists;
-//   warps 3-10  epilogue: two per TMEM lane quadrant, one per row tile (64 columns).
+//   warp 3      idle (completes warpgroup 0, which gives registers to the epilogue);
+//   warps 4-11  epilogue: two per TMEM lane quadrant, one per row tile (64 columns).
 //               The INT32 TMEM tiles are preset to the bits of 2^23 + 2^22, so after the
 //               MMA adds the tile dot the 32 bits read back ARE the float 2^23 + 2^22 +
 //               dot (exact: |dot| <= 64*128*128 < 2^22); a packed f32x2 add recovers the
@@ -55,10 +56,19 @@ constexpr int STEP_BYTES = A_BYTES + 2 * W_BYTES;
 constexpr int GS = 2;               // K steps per pipeline stage and per TMEM group
 constexpr int STAGE = GS * STEP_BYTES;
 constexpr int NS = 6;               // shared-memory stages
-constexpr int EPI_WARP0 = 3;
+constexpr int EPI_WARP0 = 4;        // warpgroup 0: producer, MMA issuer, scheduler, one idle warp
 constexpr int NEPI = 8;             // epilogue warps: 4 lane quadrants x (NEPI / 4) column slices
 constexpr int CW = 128 / (NEPI / 4);  // columns of a step one epilogue warp rescales
+constexpr int CH = CW >= 64 ? 32 : 16;  // columns per TMEM load of the rescale pipeline
 constexpr int THREADS = (EPI_WARP0 + NEPI) * 32;
+// Registers after the role split (setmaxnreg works per warpgroup): warpgroup 0 drops to
+// AUX_REGS and the two epilogue warpgroups grow to EPI_REGS.  setmaxnreg.inc draws on the
+// registers the CTA was launched with and waits until they are free, so the launcher
+// checks the compiled register count covers the split (SPLIT_REGS) before launching.
+constexpr int AUX_REGS = 40;
+constexpr int EPI_REGS = 224;
+constexpr int SPLIT_REGS = 128 * AUX_REGS + NEPI * 32 * EPI_REGS;
+static_assert(SPLIT_REGS <= 65536, "register split");
 constexpr int NG = 2;               // TMEM groups of GS 128-column step buffers
 constexpr int TMEM_COLS = 512;
 static_assert(NG * GS * 128 <= TMEM_COLS, "TMEM ring does not fit");
@@ -126,6 +136,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+template <int CH>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t* v);
+template <int CH>
+__device__ __forceinline__ void tmem_wait_ld_chunk(uint32_t* v);
+
 // 16 consecutive TMEM columns of this thread's lane (no wait).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* v) {
   asm volatile(
@@ -157,9 +172,17 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t* v) {
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+template <>
+__device__ __forceinline__ void tmem_ld_chunk<16>(uint32_t taddr, uint32_t* v) { tmem_ld16(taddr, v); }
+template <>
+__device__ __forceinline__ void tmem_ld_chunk<32>(uint32_t taddr, uint32_t* v) { tmem_ld32(taddr, v); }
+template <>
+__device__ __forceinline__ void tmem_wait_ld_chunk<16>(uint32_t* v) { tmem_wait_ld_regs16(v); }
+template <>
+__device__ __forceinline__ void tmem_wait_ld_chunk<32>(uint32_t* v) { tmem_wait_ld_regs(v); }
+
 // The same 32-bit value into 32 consecutive TMEM columns of this thread's lane (no wait),
-// as four 8-column stores: the store's source is a register vector, and eight copies of
-// the value keep the register footprint small next to the live accumulator.
+// as four 8-column stores (used once per buffer before the main loop).
 __device__ __forceinline__ void tmem_fill32(uint32_t taddr, uint32_t x) {
 #pragma unroll
   for (int u = 0; u < 32; u += 8)
@@ -204,7 +227,7 @@ struct TileHdr {
 };
 
 template <int XT, bool DUMP>
-__global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, const __grid_constant__ UmmaMaps maps) {
+__global__ void __launch_bounds__(um::THREADS) umma_kernel(const RowsArgs a, const __grid_constant__ UmmaMaps maps) {
   using namespace um;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -267,6 +290,10 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
   for (int c = tid; c < n_tc; c += THREADS) sx_s[c] = a.sx ? __ldg(a.sx + c) : 1.0f;
   __syncthreads();
   bool ok = true;
+  if (warp < EPI_WARP0)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(AUX_REGS));
+  else
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(EPI_REGS));
 
   if (warp == 2) {
     // ================================================================ scheduler
@@ -408,7 +435,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
         }
       }
     }
-  } else {
+  } else if (warp >= EPI_WARP0) {
     // ================================================================ epilogue
     const int ew = warp - EPI_WARP0;
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
@@ -440,7 +467,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
       float2 acc[CW / 2];
 #pragma unroll
       for (int e = 0; e < CW / 2; ++e) acc[e] = make_float2(0.0f, 0.0f);
-      static_assert(GS == 2 && CW % 16 == 0, "the rescale pipeline below is written for 2-step groups");
+      static_assert(GS == 2 && CW % CH == 0, "the rescale pipeline below is written for 2-step groups");
       for (int c0 = 0; c0 < n_tc; c0 += GS, ++grp) {
         const uint32_t gb = grp % NG;
         const bool two = c0 + 1 < n_tc;
@@ -453,20 +480,23 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
         const uint32_t t0 = tbase + gb * GS * 128;  // step s, half u at t0 + s * 128 + u * 32
         if (ok && !mbar_wait_bounded(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
         tc_fence_after();
-        // 16-column chunks (step s = i / CPS, columns 16 * (i % CPS)), each chunk's load
+        // CH-column chunks (step s = i / CPS, columns CH * (i % CPS)), each chunk's load
         // issued before the previous chunk's rescale so the TMEM latency overlaps FP work
-        constexpr int CPS = CW / 16;  // chunks per step
-        uint32_t v[2][16];
-        tmem_ld16(t0, v[0]);
-        tmem_wait_ld_regs16(v[0]);
+        constexpr int CPS = CW / CH;  // chunks per step
+        uint32_t v[2][CH];
+        tmem_ld_chunk<CH>(t0, v[0]);
+        tmem_wait_ld_chunk<CH>(v[0]);
 #pragma unroll
         for (int i = 0; i < GS * CPS; ++i) {
-          const uint32_t ti = t0 + (i / CPS) * 128 + (i % CPS) * 16;
-          if (i + 1 < GS * CPS) tmem_ld16(t0 + ((i + 1) / CPS) * 128 + ((i + 1) % CPS) * 16, v[(i + 1) & 1]);
-          tmem_fill16(ti, magic8);
-          rescale16<DUMP>(acc + (i % CPS) * 8, v[i & 1], (i / CPS) ? sc1 : sc0, a.partials, (i / CPS) ? p1 : p0, row,
-                          a.n_rows, (col & 63) + (i % CPS) * 16);
-          if (i + 1 < GS * CPS) tmem_wait_ld_regs16(v[(i + 1) & 1]);
+          const uint32_t ti = t0 + (i / CPS) * 128 + (i % CPS) * CH;
+          if (i + 1 < GS * CPS) tmem_ld_chunk<CH>(t0 + ((i + 1) / CPS) * 128 + ((i + 1) % CPS) * CH, v[(i + 1) & 1]);
+#pragma unroll
+          for (int hh = 0; hh < CH / 16; ++hh) {
+            tmem_fill16(ti + hh * 16, magic8);
+            rescale16<DUMP>(acc + (i % CPS) * (CH / 2) + hh * 8, v[i & 1] + hh * 16, (i / CPS) ? sc1 : sc0,
+                            a.partials, (i / CPS) ? p1 : p0, row, a.n_rows, (col & 63) + (i % CPS) * CH + hh * 16);
+          }
+          if (i + 1 < GS * CPS) tmem_wait_ld_chunk<CH>(v[(i + 1) & 1]);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -544,6 +574,10 @@ static int launch_umma_t(const RowsArgs& a, const UmmaMaps& maps, cudaStream_t s
   TQ_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && !(configured & (1ull << dev))) {
     TQ_CUDA_TRY(cudaFuncSetAttribute(umma_kernel<XT, DUMP>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    cudaFuncAttributes fa;
+    TQ_CUDA_TRY(cudaFuncGetAttributes(&fa, umma_kernel<XT, DUMP>));
+    if ((int64_t)fa.numRegs * um::THREADS < um::SPLIT_REGS)  // the register split could never complete
+      return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: compiled register count too small for the warp split");
     configured |= 1ull << dev;
   }
   // more than half the SM's shared memory: one CTA (and its 512 TMEM columns) per SM
