@@ -22,7 +22,8 @@ tiles kept BF16 (uniformly chosen), the rest INT8 with one scale per tile.
 ``--impl reference`` times that CPU restatement alone: the reference's own GEMM is a
 Triton GPU kernel that needs the reference checkout, and its CPU torch path covers
 only the quantizer and the packer.  ``--workload decode`` measures config 1 (one
-q_proj-shaped MixedLinear, 16 decode tokens) in GB/s instead.
+q_proj-shaped MixedLinear, 16 decode tokens) in GB/s instead; ``--workload gemm``
+times one mixed GEMM launch of ``--shape`` (the case the kernel profiles capture).
 
 Multi-GPU (torchrun): every rank runs its own replica of the workload (weak scaling);
 the step time is the max over ranks.
@@ -50,6 +51,7 @@ LLAMA3B = dict(hidden=3072, inter=8192, heads=24, kv_heads=8, head_dim=128, rope
 TOKENS = (4, 2048)
 KEEP = 0.05
 METRIC_PREFILL = "tile-GEMM TOPS: Llama-3.2-3B decoder block prefill (4x2048 tokens), 4 MixedLinear forwards"
+GEMM_PROFILE = "umma_kernel_gate_up_8192x16384x3072.md"
 
 
 def _peaks():
@@ -57,6 +59,18 @@ def _peaks():
         return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
     except Exception:
         return {}
+
+
+def _profile_traffic(summary: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded by
+    an ncu capture in profiles/<summary> as a line `traffic_bytes_per_launch: N`."""
+    try:
+        for line in (ROOT / "profiles" / summary).read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip().split()[0]))
+    except Exception:
+        pass
+    return None
 
 
 # ---------------------------------------------------------------- workload pieces
@@ -359,7 +373,7 @@ def run_prefill(args, ws, rank, device):
         "roofline": {"kernel": "mixed GEMM, stacked gate/up (8192 x 16384 x 3072)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                      "frac": round(achieved / peak, 3), "peak_source": peak_src, "ops_per_launch": k_ops,
-                     "launch_ms": round(k_ms, 4), "traffic": None,
+                     "launch_ms": round(k_ms, 4), "traffic": _profile_traffic(GEMM_PROFILE),
                      "frac_of_bf16_measured": round(achieved / _peaks().get("bf16_tflops", 1639.7), 3)},
         "e2e": {"value": round(ws * ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": hidden.numel() * 2, "d2h_bytes_per_step": hidden.numel() * 2,
@@ -436,6 +450,60 @@ def run_decode(args, ws, rank, device):
     }
 
 
+def run_gemm(args, ws, rank, device):
+    """One mixed tile GEMM launch per step (activations already quantized), the shape
+    given by --shape ROWSxMxK (default: the stacked gate/up GEMM of config 2)."""
+    import tilequant_b200 as tq
+    from tests.golden import inputs as I
+    from tilequant_b200 import _native as N
+
+    rows, m, k = (int(v) for v in args.shape.lower().split("x"))
+    w = I.weight(m, k, 3).to(device)
+    n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
+    fp16 = I.keep_ids(n_tr, n_tc, args.keep, 4)
+    pack = tq.pack_weight_from_tile_ids(w, n_tr=n_tr, n_tc=n_tc, int8_tile_ids=I.complement_ids(fp16, n_tr * n_tc),
+                                        fp16_tile_ids=fp16, cfg=_cfg())
+    x = I.activations(rows, k, 5).to(device)
+    q, sx = tq.quantize_activation_tile_absmax(x)
+    kw = dict(x_fp=x, x_int8=q, sx=sx, int8_tiles=pack.int8_tiles, int8_scales=pack.int8_scales,
+              int8_tile_ids=pack.int8_tile_ids, int8_row_ptr=pack.int8_row_ptr, fp16_tiles=pack.fp16_tiles,
+              fp16_tile_ids=pack.fp16_tile_ids, fp16_row_ptr=pack.fp16_row_ptr, M=m, K=k, n_tr=n_tr, n_tc=n_tc,
+              out_dtype=torch.bfloat16)
+    flush = torch.empty(int(256e6) // 4, device=device, dtype=torch.float32)
+    out = torch.empty((rows, m), device=device, dtype=torch.bfloat16)
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            tq.gemm_mixed_rows_splitk(out=out, **kw)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        launches0 = N.kernel_launches()
+        evs = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(args.steps)]
+        with ClockSampler(device.index) as clocks:
+            for e0, e1 in evs:
+                flush.zero_()
+                e0.record()
+                tq.gemm_mixed_rows_splitk(out=out, **kw)
+                e1.record()
+            torch.cuda.synchronize()
+        launches = N.kernel_launches() - launches0
+        _barrier(ws)
+    ms = _max_over_ranks(statistics.median(e0.elapsed_time(e1) for e0, e1 in evs), ws)
+    ops = 2 * rows * m * k
+    peak, peak_src = _int8_peak(device)
+    achieved = ops / (ms * 1e-3) / 1e12
+    return {
+        "metric": f"mixed tile GEMM TOPS ({rows}x{m}x{k}, {args.keep:.0%} BF16 tiles)", "value": round(ws * achieved, 1),
+        "unit": "TOPS", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16, f32 accumulate",
+        "data": "synthetic (seeded random init)",
+        "config": {"workload": "one mixed GEMM launch", "rows": rows, "M": m, "K": k, "keep_bf16": args.keep,
+                   "l2": "flushed (256 MB write) between timed steps"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+                     "frac": round(achieved / peak, 3), "peak_source": peak_src, "traffic": None},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
+
+
 def run_reference(args, ws, rank):
     """CPU restatement of the reference (oracle/) on a bounded sample of config 2."""
     if rank != 0:
@@ -473,7 +541,9 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["prefill", "decode"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "gemm"], default="prefill")
+    ap.add_argument("--shape", default="8192x16384x3072", help="ROWSxMxK of --workload gemm")
+    ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")
     args = ap.parse_args()
     ws, rank, local = _dist()
@@ -490,7 +560,8 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    line = run_decode(args, ws, rank, device) if args.workload == "decode" else run_prefill(args, ws, rank, device)
+    run = {"decode": run_decode, "gemm": run_gemm, "prefill": run_prefill}[args.workload]
+    line = run(args, ws, rank, device)
     if ws > 1:
         import torch.distributed as dist
 

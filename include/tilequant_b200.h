@@ -93,7 +93,10 @@ TQ_API int tq_quantize_act(const void* x, int x_dtype, int64_t n_rows, int64_t k
 /* ---------------------------------------------------------------- mixed GEMM
  * out[n, o] for n < n_rows, o < m (out features), k in features:
  *   per row tile r and split s (of split_k), INT8 tiles in ascending column order:
- *     acc = acc + f32(i32 tile dot) * (sx[c] * sw[t])   (separately rounded mul, add)
+ *     acc = acc + f32(i32 tile dot) * (sx[c] * sw[t])
+ *   (the row kernel rounds the multiply and the add separately, as the reference's
+ *   kernel does under the Triton interpreter; the tcgen05 kernel fuses them, as
+ *   compiled Triton does; the two differ by at most 1 ulp of the output dtype)
  *   then BF16/F16 tiles: acc += f32 dot(x_fp tile, W tile);
  *   split partials summed in split order; out = dtype(acc); with bias:
  *   out = dtype(f32(out) + f32(bias[o])).
