@@ -16,6 +16,7 @@ import pytest
 import torch
 
 import tilequant_b200 as tq
+from tilequant_b200 import _native as N
 from oracle import oracle as O
 from tests.golden import inputs as I
 from tests.helpers import assert_close_with_bias, assert_within_ulp, from_torch16, to_torch16, ulp_dist16
@@ -220,6 +221,53 @@ def test_gemm_int8_only_bit_exact_vs_oracle(cuda_device, rows, m, k, split):
     np.testing.assert_array_equal(y, ref)
 
 
+@pytest.mark.parametrize("rows,m,k,split", [(1, 64, 64, 1), (16, 3072, 3072, 8), (7, 200, 136, 3), (16, 512, 1024, 5),
+                                            (3, 1000, 4160, 8), (16, 192, 9000, 2)])
+def test_decode_kernel_int8_only_bit_exact_vs_oracle(cuda_device, rows, m, k, split):
+    """The decode kernel (algo 3) reproduces the reference arithmetic exactly, like the
+    split-K row kernel, for ragged and unaligned shapes and for more INT8 tiles per warp
+    than it keeps in flight at once."""
+    x = I.activations(rows, k, 500 + rows, outliers=2)
+    w = I.weight(m, k, 501 + m)
+    n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
+    p = _int8_only_pack(w, n_tr, n_tc)
+    y = from_torch16(_run_gemm(I.bits(x), p, m, k, split, None, algo=N.TQ_ALGO_GEMV))
+    q, sx = O.quantize_act(I.bits(x))
+    pk = O.pack(I.bits(w), n_tr, n_tc, np.arange(n_tr * n_tc), np.arange(0))
+    ref = O.gemm(q, sx, pk, I.bits(x), m, k, split_k=split, use_fma=False)
+    np.testing.assert_array_equal(y, ref)
+
+
+@pytest.mark.parametrize("rows,m,k,keep,split", [(16, 3072, 3072, 0.01, None), (5, 320, 384, 0.1, 4),
+                                                 (16, 448, 8250, 0.3, 8), (1, 64, 200, 1.0, 2)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_decode_kernel_identical_to_row_kernel(cuda_device, rows, m, k, keep, split, fused):
+    if fused and split is not None and split > 8:
+        pytest.skip("the decode kernel takes up to 8 splits")
+    """Decode kernel and split-K row kernel at the same split: the same arithmetic in the
+    same order, so bit-identical outputs (with 16-bit tiles, bias, fused quantization)."""
+    x = I.activations(rows, k, 510 + rows, outliers=2).to(DEV)
+    w = I.weight(m, k, 511)
+    n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
+    fp16 = I.keep_ids(n_tr, n_tc, keep, 512)
+    p = tq.pack_weight_from_tile_ids(w.to(DEV), n_tr=n_tr, n_tc=n_tc, int8_tile_ids=I.complement_ids(fp16, n_tr * n_tc),
+                                     fp16_tile_ids=fp16, cfg=cfg())
+    b = I.weight(1, m, 513, std=0.3).reshape(-1).to(DEV)
+    if split is None:
+        split = tq.select_split_k(n_tr=n_tr, n_tc=n_tc, n_rows=rows, device=torch.device(DEV), fused=fused)
+    kw = dict(int8_tiles=p.int8_tiles, int8_scales=p.int8_scales, int8_tile_ids=p.int8_tile_ids,
+              int8_row_ptr=p.int8_row_ptr, fp16_tiles=p.fp16_tiles, fp16_tile_ids=p.fp16_tile_ids,
+              fp16_row_ptr=p.fp16_row_ptr, M=m, K=k, n_tr=n_tr, n_tc=n_tc, out_dtype=torch.bfloat16, bias=b,
+              split_k=split)
+    q, sx = tq.quantize_activation_tile_absmax(x)
+    rows_y = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, algo=N.TQ_ALGO_ROWS, **kw)
+    if fused:
+        y = tq.gemm_mixed_fused_quant(x_fp=x, **kw)
+    else:
+        y = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, algo=N.TQ_ALGO_GEMV, **kw)
+    assert torch.equal(y.view(torch.int16), rows_y.view(torch.int16))
+
+
 @pytest.mark.parametrize("rows", [1, 16, 40, 200])
 def test_int32_partials_bit_exact(cuda_device, rows):
     k, m = 448, 320
@@ -297,8 +345,7 @@ def test_mixed_linear_forward_matches_oracle(cuda_device, rows):
     assert y.shape == (1, rows, 320) and y.dtype == torch.bfloat16
     q, sx = O.quantize_act(I.bits(x))
     pk = O.pack(I.bits(w), 5, 6, I.complement_ids(fp16, 30).numpy(), fp16.numpy())
-    split = 1 if rows > 64 else tq.select_split_k(n_tr=5, n_tc=6, n_rows=rows, device=torch.device(DEV),
-                                                  fused=rows <= 64)
+    split = 1 if rows > 64 else tq.select_split_k(n_tr=5, n_tc=6, n_rows=rows, device=torch.device(DEV))
     ref = O.gemm(q, sx, pk, I.bits(x), 320, 384, split_k=split, bias_bits=from_torch16(b))
     assert_close_with_bias(from_torch16(y.reshape(rows, 320)), ref, from_torch16(b), f"rows={rows}")
 

@@ -17,7 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libtilequant_b200.so"
 
 TQ_OK, TQ_ERR_INVALID, TQ_ERR_UNSUPPORTED, TQ_ERR_CUDA, TQ_ERR_TIMEOUT = range(5)
 TQ_DTYPE_BF16, TQ_DTYPE_F16 = 0, 1
-TQ_ALGO_AUTO, TQ_ALGO_ROWS, TQ_ALGO_UMMA = 0, 1, 2
+TQ_ALGO_AUTO, TQ_ALGO_ROWS, TQ_ALGO_UMMA, TQ_ALGO_GEMV = 0, 1, 2, 3
 ABI_VERSION = 1
 
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int

@@ -8,6 +8,8 @@ int tq_launch_rows(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st, int
 int tq_umma_supported(int64_t n_rows, int64_t m, int64_t k, const int8_t* x_i8, int64_t ld_x8, const void* x_fp,
                       int64_t ld_xfp, const void* w8, const void* w16);
 int tq_launch_umma(const tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
+int tq_gemv_supported(const tq::RowsArgs& a);
+int tq_launch_gemv(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
@@ -77,6 +79,10 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
     if (!tq_umma_supported(n_rows, m, k, x_i8, ld_x8, x_fp, ld_xfp, int8_tiles, fp16_tiles))
       return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: unsupported shape or alignment");
     return tq_launch_umma(a, n_tr, fp_dtype, st);
+  }
+  if (algo == TQ_ALGO_GEMV || (algo == TQ_ALGO_AUTO && tq_gemv_supported(a))) {
+    if (!tq_gemv_supported(a)) return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: needs <= 16 rows, aligned rows");
+    return tq_launch_gemv(a, n_tr, fp_dtype, st);
   }
   if (algo != TQ_ALGO_AUTO && algo != TQ_ALGO_ROWS) return tq_set_error(TQ_ERR_INVALID, "unknown algo");
   return tq_launch_rows(a, n_tr, fp_dtype, st, t16);

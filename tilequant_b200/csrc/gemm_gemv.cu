@@ -1,0 +1,243 @@
+// Decode-sized mixed INT8/BF16 64x64 tile GEMM (up to 16 activation rows), sm_100a.
+//
+// Reference: src/kernels/triton/gemm_rows_splitk_64x64.py:78-190 with SPLIT_K = S:
+// split s of row tile r owns positions [b + cnt*s/S, b + cnt*(s+1)/S) of the row's INT8
+// list and of its 16-bit list; acc = acc + f32(i32 tile dot) * (sx[c] * sw[pos]) (mul
+// and add rounded separately) in ascending column order, then acc += dot(x, W16^T);
+// the split partials are added in split order 0..S-1, rounded, then the bias.
+//
+// Decode is a latency problem: a 3072 x 3072 layer streams 9.75 MB, about 1.5 us of
+// HBM time, so every dependent round trip to memory counts.  Layout for that:
+//   * one CTA per (row tile r, 16-column slice m of its 64 output columns): n_tr * 4
+//     CTAs, and warp s of the CTA is split s -- the reference's split-K becomes a
+//     warp split with an in-CTA, in-order shared-memory reduction, no clusters;
+//   * operands go from global memory straight into MMA fragments: a thread's share of
+//     a 64x64 INT8 tile slice is two 16-byte loads, so all of a warp's tiles are in
+//     flight at once with no shared-memory staging, no barriers and no bulk-copy
+//     engine round trip (a plain 16-byte load returns in about a quarter of the time
+//     of a bulk copy here);
+//   * everything that depends only on the weights (row pointers, tile ids, scales and
+//     the weight fragments themselves) is loaded before griddepcontrol.wait, so under
+//     programmatic dependent launch it overlaps the kernel that produces the
+//     activations; only the activation loads follow the wait;
+//   * swap-AB mma.sync m16n8k32 (weights = M side, tokens = N side in two blocks of 8)
+//     with the k order permuted identically for both operands (every thread holds 16
+//     contiguous bytes of a row), so the exact INT32 dot is unchanged.
+// Quantization stays a separate launch: quantizing inside this kernel repeats it in
+// every CTA (n_tr * 4 times per column tile), which cost more than the launch saved.
+// The results are bit-identical to the split-K row kernel at the same split.
+#include "common.cuh"
+#include "gemm_args.cuh"
+#include "tma.cuh"
+
+namespace tq {
+
+namespace gv {
+constexpr int U = 6;        // INT8 tiles per warp the automatic split aims for
+constexpr int MAX_S = 8;    // splits (warps) per CTA
+constexpr int PSTRIDE = 260;  // floats per split partial (16 columns x 16 tokens, padded)
+}  // namespace gv
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// 16 bytes at byte offset `off` of a row of `len` valid bytes; zeros past the end.
+// `vec`: the row start is 16-byte aligned (else bytes are read one by one).
+__device__ __forceinline__ uint4 ldg16_row(const uint8_t* row, int off, int len, bool vec) {
+  if (vec && off + 16 <= len) return ldg16(row + off);
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  for (int e = 0; e < 16 && off + e < len; ++e) w[e >> 2] |= (uint32_t)row[off + e] << ((e & 3) * 8);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ float i2f_exact_gv(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);  // exact for |v| < 2^22
+}
+
+// Weight fragments, column ids and weight scales of up to N consecutive INT8 tiles.
+template <int N>
+struct WChunk {
+  uint4 wl[N], wh[N];
+  int col[N];
+  float sw[N];
+  int n;
+};
+
+template <int N>
+__device__ __forceinline__ void load_w(const RowsArgs& a, WChunk<N>& c, int p0, int hi8, int wr, int t) {
+  c.n = max(0, min(N, hi8 - p0));
+#pragma unroll
+  for (int u = 0; u < N; ++u) {
+    if (u < c.n) {
+      const int8_t* tile = a.w8 + (int64_t)(p0 + u) * 4096;
+      c.wl[u] = ldg16(tile + wr * 64 + 16 * t);
+      c.wh[u] = ldg16(tile + (wr + 8) * 64 + 16 * t);
+      c.col[u] = __ldg(a.ids8 + p0 + u);  // tile id; the column is taken when it is needed
+      c.sw[u] = a.s8 ? __ldg(a.s8 + p0 + u) : 1.0f;
+    }
+  }
+}
+
+// Activations of a chunk and its MMAs.
+template <int N>
+__device__ __forceinline__ void run_chunk(const RowsArgs& a, const WChunk<N>& c, float (&acc)[2][4], int g, int t) {
+  uint4 xa[N][2];
+  float sc[N];
+  int col[N];  // the loads of the whole chunk are issued before any of them is used
+#pragma unroll
+  for (int u = 0; u < N; ++u) col[u] = c.col[u] % a.n_tc;
+#pragma unroll
+  for (int u = 0; u < N; ++u) {
+    if (u < c.n) {
+#pragma unroll
+        for (int nb = 0; nb < 2; ++nb) {
+          const int row = nb * 8 + g;
+          xa[u][nb] = row < a.n_rows ? ldg16_row(reinterpret_cast<const uint8_t*>(a.x_i8) + (int64_t)row * a.ld_x8,
+                                                 col[u] * 64 + 16 * t, a.K, a.a8_vec != 0)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+        }
+        sc[u] = (a.sx ? __ldg(a.sx + col[u]) : 1.0f) * c.sw[u];  // (sx * sw) in f32, reference :135-137
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < N; ++u) {
+    if (u < c.n) {
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        int d[4] = {0, 0, 0, 0};
+        mma_s8_16832(d, c.wl[u].x, c.wh[u].x, c.wl[u].y, c.wh[u].y, xa[u][nb].x, xa[u][nb].y);
+        mma_s8_16832(d, c.wl[u].z, c.wh[u].z, c.wl[u].w, c.wh[u].w, xa[u][nb].z, xa[u][nb].w);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[nb][q] = __fadd_rn(acc[nb][q], __fmul_rn(i2f_exact_gv(d[q]), sc[u]));
+      }
+    }
+  }
+}
+
+template <int XT>
+__global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs a) {
+  constexpr int UC = 6;  // INT8 tiles per chunk
+
+  using namespace gv;
+  __shared__ float part[MAX_S * PSTRIDE];
+  const int S = blockDim.x >> 5;
+  const int r = blockIdx.x >> 2, m = blockIdx.x & 3;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int wr = 16 * m + g;  // this thread's weight rows in the tile: wr and wr + 8
+
+  grid_dep_launch();  // the next kernel may start its own weight-side prologue
+
+  const int b8 = __ldg(a.rp8 + r), c8 = __ldg(a.rp8 + r + 1) - b8;
+  const int lo8 = b8 + (c8 * warp) / S, hi8 = b8 + (c8 * (warp + 1)) / S;
+  int lo16 = 0, hi16 = 0;
+  if (a.has_fp16) {
+    const int b16 = __ldg(a.rp16 + r), c16 = __ldg(a.rp16 + r + 1) - b16;
+    lo16 = b16 + (c16 * warp) / S;
+    hi16 = b16 + (c16 * (warp + 1)) / S;
+  }
+
+  float acc[2][4];
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[nb][q] = 0.0f;
+
+  // INT8 tiles in chunks of UC per warp, every load of a chunk in flight together; the
+  // first chunk's weights are requested before the wait for the preceding kernel.
+  WChunk<UC> ch;
+  load_w(a, ch, lo8, hi8, wr, t);
+  grid_dep_wait();  // activations (and their scales) come from the preceding kernel
+  run_chunk(a, ch, acc, g, t);
+#pragma unroll 1
+  for (int p0 = lo8 + UC; p0 < hi8; p0 += UC) {
+    load_w(a, ch, p0, hi8, wr, t);
+    run_chunk(a, ch, acc, g, t);
+  }
+
+  // 16-bit tiles of this split, each as two 32-column halves (m16n8k16, FP32 accumulate)
+#pragma unroll 1
+  for (int p = lo16; p < hi16; ++p) {
+    const uint16_t* tile = reinterpret_cast<const uint16_t*>(a.w16) + (int64_t)p * 4096;
+    const int c = __ldg(a.ids16 + p) % a.n_tc;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const uint4 wlo = ldg16(tile + wr * 64 + half * 32 + 8 * t);
+      const uint4 whi = ldg16(tile + (wr + 8) * 64 + half * 32 + 8 * t);
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb) {
+        const int row = nb * 8 + g;
+        uint4 xb = make_uint4(0u, 0u, 0u, 0u);
+        if (row < a.n_rows)
+          xb = ldg16_row(reinterpret_cast<const uint8_t*>(a.x_fp) + (int64_t)row * a.ld_xfp * 2,
+                         (c * 64 + half * 32 + 8 * t) * 2, a.K * 2, a.afp_vec != 0);
+        mma_16816<XT>(acc[nb], wlo.x, whi.x, wlo.y, whi.y, xb.x, xb.y);
+        mma_16816<XT>(acc[nb], wlo.z, whi.z, wlo.w, whi.w, xb.z, xb.w);
+      }
+    }
+  }
+
+  // split partials: column j = g + 8 (q >> 1) of the slice, token 8 nb + 2 t + (q & 1)
+  float* mine = part + warp * PSTRIDE;
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) mine[(g + 8 * (q >> 1)) * 16 + nb * 8 + 2 * t + (q & 1)] = acc[nb][q];
+  __syncthreads();
+  for (int e = tid; e < 256; e += blockDim.x) {
+    const int j = e >> 4, tok = e & 15;
+    float v = part[e];
+    for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
+    const int cc = r * 64 + 16 * m + j;
+    if (tok < a.n_rows && cc < a.M && a.out) {
+      const int ot = a.out_dtype;
+      uint16_t y = f2h(v, ot);
+      if (a.bias) y = f2h(h2f(y, ot) + h2f(reinterpret_cast<const uint16_t*>(a.bias)[cc], ot), ot);
+      reinterpret_cast<uint16_t*>(a.out)[(int64_t)tok * a.ldo + cc] = y;
+    }
+  }
+}
+
+}  // namespace tq
+
+using namespace tq;
+
+// Split the decode kernel uses when none is given: enough warps that each holds at most
+// gv::U INT8 tiles of a full row (all its loads in flight at once), a power of two.
+int tq_gemv_split(int n_tc) {
+  int s = 1;
+  while (s < gv::MAX_S && (n_tc + s - 1) / s > gv::U) s *= 2;
+  return s;
+}
+
+int tq_gemv_supported(const RowsArgs& a) {
+  return a.n_rows > 0 && a.n_rows <= 16 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
+}
+
+int tq_launch_gemv(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st) {
+  a.n_tr = n_tr;
+  a.a8_vec = a.x_i8 && ((uintptr_t)a.x_i8 & 15) == 0 && (a.ld_x8 & 15) == 0;
+  a.afp_vec = a.x_fp && ((uintptr_t)a.x_fp & 15) == 0 && ((a.ld_xfp * 2) & 15) == 0;
+  if (a.split == 0) a.split = tq_gemv_split(a.n_tc);
+  if (a.split < 1 || a.split > gv::MAX_S) return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: split_k must be in 1..8");
+  if ((int64_t)n_tr * 4 > INT32_MAX) return tq_set_error(TQ_ERR_INVALID, "too many row tiles");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_tr * 4), 1, 1);
+  cfg.blockDim = dim3(32 * a.split, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (tq_pdl_enabled()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  if (fp_dtype == TQ_DTYPE_BF16) {
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<TQ_DTYPE_BF16>, a));
+  } else {
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<TQ_DTYPE_F16>, a));
+  }
+  tq_count_launch();
+  return TQ_OK;
+}

@@ -183,12 +183,38 @@ __global__ void __launch_bounds__(160) rows_kernel(const RowsArgs a, const __gri
   if (warp == 4) {
     // ================================================================ producer
     grid_dep_wait();  // activations and their scales come from the preceding kernel
+    // With tensor maps, the activation copies of the first ring's worth of steps go out
+    // before the scales are read, so the two global round trips overlap; the stage's
+    // arrival (which publishes its scale) follows the scale.
+    const int early = tma_x ? min(nitems, NS) : 0;
+    if (lane == 0) {
+      for (int i = 0; i < early; ++i) {
+        const int pos = it_pos[i], c = it_c[i];
+        uint8_t* adst = stages + i * SB + C::W_BYTES;
+        if (pos >= 0 && fused) {
+          mbar_add_tx(&full[i], BN * 128);
+          tma_load_2d(adst, &maps.xfp_full, c * 64, n0, &full[i]);
+        } else if (pos >= 0) {
+          mbar_add_tx(&full[i], BN * 64);
+          tma_load_2d(adst, &maps.x8, c * 64, n0, &full[i]);
+        } else {
+          mbar_add_tx(&full[i], BN * 64);
+          tma_load_2d(adst, &maps.xfp_half, c * 64 + ((-pos - 1) & 1) * 32, n0, &full[i]);
+        }
+      }
+    }
     if (!fused) {
       for (int c = lane; c < a.n_tc; c += 32) sx_s[c] = a.sx ? __ldg(a.sx + c) : 1.0f;
       __syncwarp();
     }
+    if (lane == 0) {
+      for (int i = 0; i < early; ++i) {
+        if (it_pos[i] >= 0 && !fused) st_scale[i] = sx_s[it_c[i]] * it_s[i];  // (sx * sw) in f32, ref :135-137
+        mbar_arrive(&full[i]);
+      }
+    }
 #pragma unroll 1
-    for (int i = 0; i < nitems; ++i) {
+    for (int i = early; i < nitems; ++i) {
       const int stg = i % NS;
       const int pos = it_pos[i];
       if (i >= NS) {
@@ -551,8 +577,15 @@ int tq_launch_rows(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st, int64_t
 }
 
 // The split and row tiles per CTA the rows kernel picks for a shape (split_k = 0).
+int tq_gemv_split(int n_tc);
+
 extern "C" int tq_gemm_rows_plan(int64_t n_rows, int n_tr, int n_tc, int fp_dtype, int fused, int* split, int* rows_per_cta) {
   if (n_rows <= 0 || n_tr <= 0 || n_tc <= 0 || !split || !rows_per_cta) return tq_set_error(TQ_ERR_INVALID, "bad plan query");
+  if (n_rows <= 16) {  // the decode kernel (TQ_ALGO_GEMV)
+    *split = tq_gemv_split(n_tc);
+    *rows_per_cta = 1;
+    return TQ_OK;
+  }
   const int nb = rows_nb(n_rows);
   const int n_blocks = (int)((n_rows + 8 * nb - 1) / (8 * nb));
   int sp = 0, rpc = 1;

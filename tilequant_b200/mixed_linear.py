@@ -11,9 +11,12 @@ interchange), cfg keys and errors, calling the sm_100a kernels of this package:
 * activation-quantization sharing between siblings -- mixed_linear.py:37-111
 
 Forward, by activation row count N:
-* N <= 64 (decode): one launch, activation quantization fused into the GEMM;
 * N <= activation_row_chunk_size: quantize once (shared with sibling projections of
-  the same activation when N >= 32 in inference mode), then the GEMM;
+  the same activation when N >= 32 in inference mode), then the GEMM -- up to 16 rows
+  the decode kernel, up to 64 the split-K row kernel, above that the tcgen05 kernel
+  (the quantizer-fused GEMM, ``gemm_mixed_fused_quant``, stays available; quantizing
+  once in its own launch is faster on B200 because the fused form repeats the
+  quantization in every CTA);
 * larger: tile scales over all rows first, then quantize + GEMM per row chunk, each
   chunk writing its row slice of one output.
 All three give identical results: the scales are global over the call's rows.
@@ -28,7 +31,7 @@ from typing import Any, Dict, Optional, Tuple
 import torch
 import torch.nn as nn
 
-from .gemm import gemm_mixed_fused_quant, gemm_mixed_rows_splitk
+from .gemm import gemm_mixed_rows_splitk
 from .pack import Pack, concat_packs_along_rows
 from .quant_utils import (
     activation_tile_absmax_scales,
@@ -40,7 +43,6 @@ from .quant_utils import (
 # not depend on it).  B200's 180 GB lets prefill run in far fewer, larger launches.
 DEFAULT_ACTIVATION_ROW_CHUNK_SIZE = 16384
 ACTIVATION_QUANT_CACHE_MIN_ROWS = 32
-FUSED_QUANT_MAX_ROWS = 64
 
 
 @dataclass
@@ -181,10 +183,7 @@ class MixedLinear(nn.Module):
             raise ValueError(f"Input K mismatch: got {k_in}, expected {self.K_orig}")
         x_work = x2d.contiguous()
         out_dtype = self._out_dtype()
-        if n_rows <= FUSED_QUANT_MAX_ROWS:
-            y = gemm_mixed_fused_quant(x_fp=x_work, out_dtype=out_dtype, bias=self._out_bias(out_dtype),
-                                       **self._weights())
-        elif n_rows <= self._activation_row_chunk_size():
+        if n_rows <= self._activation_row_chunk_size():
             x_int8, sx = _quantize_shared_activation(x, x_work, self.tile_n, id(self))
             y = self._gemm_bias(x_fp=x_work, x_int8=x_int8, sx=sx)
         else:
