@@ -504,6 +504,96 @@ def run_gemm(args, ws, rank, device):
     }
 
 
+GEN_MODELS = {
+    # config 3: Llama-3.2-3B, 1 % BF16 tiles, batch 4, prompt 2048, 256 new tokens
+    "llama3b": dict(arch="llama", hidden=3072, inter=8192, layers=28, heads=24, kv_heads=8, head_dim=128,
+                    vocab=128256, tie=True, rope_theta=500000.0, keep=0.01, batch=4, prompt=2048, new=256),
+    # config 4: Qwen2.5-7B, 10 % BF16 tiles, batch 16, prompt 1024, 256 new tokens
+    "qwen7b": dict(arch="qwen2", hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_dim=128,
+                   vocab=152064, tie=False, rope_theta=1000000.0, keep=0.10, batch=16, prompt=1024, new=256),
+    # config 5: Qwen2.5-14B, 20 % BF16 tiles, batch 64, prompt 1024, 256 new tokens
+    "qwen14b": dict(arch="qwen2", hidden=5120, inter=13824, layers=48, heads=40, kv_heads=8, head_dim=128,
+                    vocab=152064, tie=False, rope_theta=1000000.0, keep=0.20, batch=64, prompt=1024, new=256),
+}
+
+
+def build_generation_model(spec, device, seed=0):
+    """Random-init decoder of the given architecture on `device` (bf16), projections
+    replaced by MixedLinear with uniformly random tile maps."""
+    from tilequant_b200.apply import apply_random_tile_maps
+
+    common = dict(hidden_size=spec["hidden"], intermediate_size=spec["inter"], num_hidden_layers=spec["layers"],
+                  num_attention_heads=spec["heads"], num_key_value_heads=spec["kv_heads"],
+                  vocab_size=spec["vocab"], tie_word_embeddings=spec["tie"], rope_theta=spec["rope_theta"],
+                  max_position_embeddings=max(4096, spec["prompt"] + spec["new"]), attn_implementation="sdpa")
+    if spec["arch"] == "llama":
+        from transformers import LlamaConfig as Cfg, LlamaForCausalLM as Model
+
+        common["head_dim"] = spec["head_dim"]
+    else:
+        from transformers import Qwen2Config as Cfg, Qwen2ForCausalLM as Model
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Model(Cfg(**common)).to(torch.bfloat16).eval()
+    apply_random_tile_maps(model, spec["keep"], seed=seed + 1, model_type=spec["arch"])
+    torch.cuda.empty_cache()
+    return model
+
+
+def run_generate(args, ws, rank, device):
+    """Configs 3-5: greedy generation with the CUDA-graph decoder; decode tokens/s,
+    TTFT and TPOT (median over the timed requests)."""
+    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
+
+    spec = dict(GEN_MODELS[args.model])
+    model = build_generation_model(spec, device)
+    B, P, T = spec["batch"], spec["prompt"], spec["new"]
+    dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=P, max_new_tokens=T, batch_size=B, device=device)
+    per_request = dec.captured_launches["prefill"] + (T - 1) * dec.captured_launches["decode"]
+    layers = spec["layers"]
+    gen = torch.Generator().manual_seed(1234)
+    prompts = [torch.randint(0, spec["vocab"], (B, P), generator=gen).pin_memory()
+               for _ in range(args.warmup + args.steps)]
+    host_out = torch.empty((B, T), dtype=torch.long).pin_memory()
+    ttft, dec_ms, tot_ms = [], [], []
+    with ClockSampler(device.index) as clocks:
+        for i, prompt in enumerate(prompts):
+            _barrier(ws)
+            torch.cuda.synchronize()
+            e0, e1, e2 = (torch.cuda.Event(True) for _ in range(3))
+            e0.record()
+            dec.prefill(prompt)
+            e1.record()
+            ids = dec.decode(T - 1)
+            e2.record()
+            host_out.copy_(ids, non_blocking=True)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                ttft.append(e0.elapsed_time(e1))
+                dec_ms.append(e1.elapsed_time(e2))
+                tot_ms.append(e0.elapsed_time(e2))
+    dec.close()
+    t_med = statistics.median(tot_ms)
+    d_med = _max_over_ranks(statistics.median(dec_ms), ws)
+    value = ws * B * (T - 1) / (d_med * 1e-3)
+    return {
+        "metric": f"decode tokens/s: {args.model} greedy generation (batch {B}, prompt {P}, {T} new tokens), "
+                  "CUDA-graph decode", "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_med, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16 projections, bf16 elsewhere",
+        "data": "synthetic (random-init weights, uniform random tile maps and token ids)",
+        "config": {"workload": f"config {'3' if args.model == 'llama3b' else ('4' if args.model == 'qwen7b' else '5')}:"
+                               f" {args.model}", "layers": layers, "keep_bf16": spec["keep"], "batch": B,
+                   "prompt": P, "new_tokens": T, "parallelism": f"replicas x{ws}",
+                   "l2": "weights (GBs) and KV cache exceed L2 every step"},
+        "ttft_ms_p50": round(statistics.median(ttft), 3), "tpot_ms_p50": round(d_med / (T - 1), 4),
+        "e2e": {"value": round(ws * B * T / (t_med * 1e-3), 1), "unit": "tokens/s (prefill + decode)",
+                "h2d_bytes_per_step": B * P * 8, "d2h_bytes_per_step": B * T * 8},
+        "gpu_launches": per_request * args.steps, "gpu_launches_per_graph": dec.captured_launches,
+        "clocks": clocks.summary(),
+    }
+
+
 def run_reference(args, ws, rank):
     """CPU restatement of the reference (oracle/) on a bounded sample of config 2."""
     if rank != 0:
@@ -541,7 +631,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["prefill", "decode", "gemm"], default="prefill")
+    ap.add_argument("--workload", choices=["prefill", "decode", "gemm", "generate"], default="prefill")
+    ap.add_argument("--model", choices=sorted(GEN_MODELS), default="llama3b", help="model of --workload generate")
     ap.add_argument("--shape", default="8192x16384x3072", help="ROWSxMxK of --workload gemm")
     ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")
@@ -560,7 +651,7 @@ def main():
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
-    run = {"decode": run_decode, "gemm": run_gemm, "prefill": run_prefill}[args.workload]
+    run = {"decode": run_decode, "gemm": run_gemm, "prefill": run_prefill, "generate": run_generate}[args.workload]
     line = run(args, ws, rank, device)
     if ws > 1:
         import torch.distributed as dist

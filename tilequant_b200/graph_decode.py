@@ -134,6 +134,8 @@ class CudaGraphGreedyDecoder:
         self._decode_logits: Optional[torch.Tensor] = None
         self.last_logits: Optional[torch.Tensor] = None
         self.prefill_captured = False
+        # kernels of this library in one replay of each graph (counted during capture)
+        self.captured_launches = {"prefill": 0, "decode": 0}
         self._prepared = False
         self._attach()
 
@@ -202,17 +204,23 @@ class CudaGraphGreedyDecoder:
             return
         torch.cuda.empty_cache()
         self.prefill_captured = self.batch_size * self.prompt_tokens <= MAX_CAPTURED_PREFILL_TOKENS
+        from ._native import kernel_launches
+
         if self.prefill_captured:
             g = torch.cuda.CUDAGraph()
+            n0 = kernel_launches()
             with torch.cuda.graph(g):
                 self._prefill_body()
+            self.captured_launches["prefill"] = kernel_launches() - n0
             self._prefill_graph = g
         else:
             self._prefill_body()
         if decode:
             g = torch.cuda.CUDAGraph()
+            n0 = kernel_launches()
             with torch.cuda.graph(g):
                 self._decode_body()
+            self.captured_launches["decode"] = kernel_launches() - n0
             self._decode_graph = g
         torch.cuda.synchronize(self.device)
         self._prepared = True
