@@ -1,0 +1,95 @@
+"""Tensor parallelism on 2 GPUs (skipped with fewer): the sharded MixedLinear decoder
+against the unsharded one, eager forward and CUDA-graph greedy decoding with the NCCL
+all-reduces captured in the graphs."""
+
+from __future__ import annotations
+
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _model(dev, qwen=False):
+    if qwen:
+        from transformers import Qwen2Config as Cfg, Qwen2ForCausalLM as Model
+
+        cfg = Cfg(hidden_size=512, intermediate_size=1280, num_hidden_layers=2, num_attention_heads=8,
+                  num_key_value_heads=2, vocab_size=500, attn_implementation="sdpa")
+    else:
+        from transformers import LlamaConfig as Cfg, LlamaForCausalLM as Model
+
+        cfg = Cfg(hidden_size=512, intermediate_size=1280, num_hidden_layers=2, num_attention_heads=8,
+                  num_key_value_heads=4, head_dim=64, vocab_size=500, attn_implementation="sdpa")
+    torch.manual_seed(0)
+    with torch.device(dev):
+        return Model(cfg).to(torch.bfloat16).eval()
+
+
+def _worker(rank, world, port, qwen, out_q):
+    import os
+
+    import torch.distributed as dist
+
+    from tilequant_b200.apply import apply_tile_maps
+    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
+    from tilequant_b200.parallel import projection_shapes, seeded_random_keep, tensor_parallel_
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    import datetime
+
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    try:
+        mtype = "qwen2" if qwen else "llama"
+        full = _model(dev, qwen)
+        keep = seeded_random_keep(0.1, 5, list(projection_shapes(full)))
+        apply_tile_maps(full, keep, model_type=mtype)
+        ids = torch.randint(0, 500, (2, 24), generator=torch.Generator().manual_seed(1)).to(dev)
+        with torch.inference_mode():
+            want = full(input_ids=ids).logits.float()
+        del full
+        model = _model(dev, qwen)
+        tensor_parallel_(model, rank, world, keep, model_type=mtype)
+        with torch.inference_mode():
+            got = model(input_ids=ids).logits.float()
+        rel = float((got - want).abs().max() / want.abs().max())
+        dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=24, max_new_tokens=12, batch_size=2, device=dev)
+        toks = dec.generate(ids.cpu()).clone()
+        dec.close()
+        gathered = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(gathered, toks)
+        same = all(torch.equal(g, toks) for g in gathered)
+        out_q.put((rank, rel, same))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("qwen", [False, True])
+def test_tensor_parallel_two_gpus(qwen):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, qwen, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, rel, same in res:
+        assert rel < 2e-2, (rank, rel)  # row-parallel partials are summed in BF16
+        assert same, rank  # every rank generates the same tokens
