@@ -517,10 +517,13 @@ GEN_MODELS = {
 }
 
 
-def build_generation_model(spec, device, seed=0):
+def build_generation_model(spec, device, seed=0, tp=None):
     """Random-init decoder of the given architecture on `device` (bf16), projections
-    replaced by MixedLinear with uniformly random tile maps."""
+    replaced by MixedLinear with uniformly random tile maps; with tp = (rank, world,
+    group), this rank's tensor-parallel shard of it (the same full model and maps on
+    every rank)."""
     from tilequant_b200.apply import apply_random_tile_maps
+    from tilequant_b200.parallel import projection_shapes, seeded_random_keep, tensor_parallel_
 
     common = dict(hidden_size=spec["hidden"], intermediate_size=spec["inter"], num_hidden_layers=spec["layers"],
                   num_attention_heads=spec["heads"], num_key_value_heads=spec["kv_heads"],
@@ -535,7 +538,11 @@ def build_generation_model(spec, device, seed=0):
     torch.manual_seed(seed)
     with torch.device(device):
         model = Model(Cfg(**common)).to(torch.bfloat16).eval()
-    apply_random_tile_maps(model, spec["keep"], seed=seed + 1, model_type=spec["arch"])
+    if tp is None:
+        apply_random_tile_maps(model, spec["keep"], seed=seed + 1, model_type=spec["arch"])
+    else:
+        keep = seeded_random_keep(spec["keep"], seed + 1, list(projection_shapes(model)))
+        tensor_parallel_(model, tp[0], tp[1], keep, group=tp[2], model_type=spec["arch"])
     torch.cuda.empty_cache()
     return model
 
@@ -546,7 +553,8 @@ def run_generate(args, ws, rank, device):
     from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
 
     spec = dict(GEN_MODELS[args.model])
-    model = build_generation_model(spec, device)
+    tp = args.tp and ws > 1
+    model = build_generation_model(spec, device, tp=(rank, ws, None) if tp else None)
     B, P, T = spec["batch"], spec["prompt"], spec["new"]
     dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=P, max_new_tokens=T, batch_size=B, device=device)
     per_request = dec.captured_launches["prefill"] + (T - 1) * dec.captured_launches["decode"]
@@ -575,19 +583,23 @@ def run_generate(args, ws, rank, device):
     dec.close()
     t_med = statistics.median(tot_ms)
     d_med = _max_over_ranks(statistics.median(dec_ms), ws)
-    value = ws * B * (T - 1) / (d_med * 1e-3)
+    t_med = _max_over_ranks(t_med, ws)
+    jobs = 1 if tp else ws  # tensor parallel: one job over all ranks; else one replica per rank
+    value = jobs * B * (T - 1) / (d_med * 1e-3)
     return {
         "metric": f"decode tokens/s: {args.model} greedy generation (batch {B}, prompt {P}, {T} new tokens), "
                   "CUDA-graph decode", "value": round(value, 1), "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_med, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16 projections, bf16 elsewhere",
+        "scaling": "strong" if tp else "weak", "vs_baseline": None,
+        "dtype": "int8 + bf16 projections, bf16 elsewhere",
         "data": "synthetic (random-init weights, uniform random tile maps and token ids)",
         "config": {"workload": f"config {'3' if args.model == 'llama3b' else ('4' if args.model == 'qwen7b' else '5')}:"
                                f" {args.model}", "layers": layers, "keep_bf16": spec["keep"], "batch": B,
-                   "prompt": P, "new_tokens": T, "parallelism": f"replicas x{ws}",
+                   "prompt": P, "new_tokens": T,
+                   "parallelism": f"tp{ws} (NCCL all-reduce after O and down)" if tp else f"replicas x{ws}",
                    "l2": "weights (GBs) and KV cache exceed L2 every step"},
         "ttft_ms_p50": round(statistics.median(ttft), 3), "tpot_ms_p50": round(d_med / (T - 1), 4),
-        "e2e": {"value": round(ws * B * T / (t_med * 1e-3), 1), "unit": "tokens/s (prefill + decode)",
+        "e2e": {"value": round(jobs * B * T / (t_med * 1e-3), 1), "unit": "tokens/s (prefill + decode)",
                 "h2d_bytes_per_step": B * P * 8, "d2h_bytes_per_step": B * T * 8},
         "gpu_launches": per_request * args.steps, "gpu_launches_per_graph": dec.captured_launches,
         "clocks": clocks.summary(),
@@ -633,6 +645,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["prefill", "decode", "gemm", "generate"], default="prefill")
     ap.add_argument("--model", choices=sorted(GEN_MODELS), default="llama3b", help="model of --workload generate")
+    ap.add_argument("--tp", action="store_true", help="--workload generate: tensor parallel over the ranks")
     ap.add_argument("--shape", default="8192x16384x3072", help="ROWSxMxK of --workload gemm")
     ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")
