@@ -52,6 +52,7 @@ TOKENS = (4, 2048)
 KEEP = 0.05
 METRIC_PREFILL = "tile-GEMM TOPS: Llama-3.2-3B decoder block prefill (4x2048 tokens), 4 MixedLinear forwards"
 GEMM_PROFILE = "umma_kernel_gate_up_8192x16384x3072.md"
+DECODE_PROFILE = "gemv_kernel_config1_16x3072x3072.md"
 
 
 def _peaks():
@@ -443,7 +444,8 @@ def run_decode(args, ws, rank, device):
                    "calls_per_step": nrot, "l2": "40 distinct weight copies per step (> 2x L2)",
                    "graph": "one CUDA graph of 40 calls per step"},
         "roofline": {"bound": "hbm", "achieved": round(gbs / ws, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(gbs / ws / hbm, 3), "traffic": None, "us_per_call": round(us, 3),
+                     "frac": round(gbs / ws / hbm, 3), "traffic": _profile_traffic(DECODE_PROFILE),
+                     "us_per_call": round(us, 3),
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "gpu_launches": per_replay * args.steps,
         "clocks": clocks.summary(),
