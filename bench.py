@@ -513,9 +513,11 @@ GEN_MODELS = {
     # config 4: Qwen2.5-7B, 10 % BF16 tiles, batch 16, prompt 1024, 256 new tokens
     "qwen7b": dict(arch="qwen2", hidden=3584, inter=18944, layers=28, heads=28, kv_heads=4, head_dim=128,
                    vocab=152064, tie=False, rope_theta=1000000.0, keep=0.10, batch=16, prompt=1024, new=256),
-    # config 5: Qwen2.5-14B, 20 % BF16 tiles, batch 64, prompt 1024, 256 new tokens
+    # config 5: Qwen2.5-14B, 20 % BF16 tiles chosen by IAA from 64 x 2048 random ids, batch 64, prompt
+    # 1024, 256 new tokens
     "qwen14b": dict(arch="qwen2", hidden=5120, inter=13824, layers=48, heads=40, kv_heads=8, head_dim=128,
-                    vocab=152064, tie=False, rope_theta=1000000.0, keep=0.20, batch=64, prompt=1024, new=256),
+                    vocab=152064, tie=False, rope_theta=1000000.0, keep=0.20, batch=64, prompt=1024, new=256,
+                    calib="iaa", calib_seqs=64, calib_len=2048),
 }
 
 
@@ -540,7 +542,27 @@ def build_generation_model(spec, device, seed=0, tp=None):
     torch.manual_seed(seed)
     with torch.device(device):
         model = Model(Cfg(**common)).to(torch.bfloat16).eval()
-    if tp is None:
+    if spec.get("calib") == "iaa":
+        # IAA tile importance on the GPU over seeded random token ids, then the top tiles
+        # per projection stay 16-bit and the INT8 scales use the IAA search
+        from tilequant_b200.apply import apply_tile_maps, default_cfg
+        from tilequant_b200.calibrate import collect_iaa_tile_scores_with_channel_stats, keep_ids_from_scores
+        from tilequant_b200.rules import TARGET_SUFFIXES
+
+        gen = torch.Generator().manual_seed(seed + 7)
+        per = 4
+        batches = [{"input_ids": torch.randint(0, spec["vocab"], (per, spec["calib_len"]), generator=gen)}
+                   for _ in range(spec["calib_seqs"] // per)]
+        scores, stats = collect_iaa_tile_scores_with_channel_stats(
+            model, batches, lambda n: n.endswith(TARGET_SUFFIXES), {"calib": {}})
+        kept = keep_ids_from_scores(scores, spec["keep"])
+        cfg = default_cfg(quant_style="iaa")
+        if tp is None:
+            apply_tile_maps(model, kept, cfg, model_type=spec["arch"], iaa_channel_stats=stats)
+        else:
+            tensor_parallel_(model, tp[0], tp[1], lambda n, n_tr, n_tc: kept[n], cfg, group=tp[2],
+                             model_type=spec["arch"], iaa_channel_stats=stats)
+    elif tp is None:
         apply_random_tile_maps(model, spec["keep"], seed=seed + 1, model_type=spec["arch"])
     else:
         keep = seeded_random_keep(spec["keep"], seed + 1, list(projection_shapes(model)))
@@ -558,7 +580,10 @@ def run_generate(args, ws, rank, device):
     tp = args.tp and ws > 1
     model = build_generation_model(spec, device, tp=(rank, ws, None) if tp else None)
     B, P, T = spec["batch"], spec["prompt"], spec["new"]
+    from tilequant_b200 import _native as N
+
     dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=P, max_new_tokens=T, batch_size=B, device=device)
+    # graph replays launch the captured kernels; an uncaptured (eager) prefill is counted live
     per_request = dec.captured_launches["prefill"] + (T - 1) * dec.captured_launches["decode"]
     layers = spec["layers"]
     gen = torch.Generator().manual_seed(1234)
@@ -566,14 +591,18 @@ def run_generate(args, ws, rank, device):
                for _ in range(args.warmup + args.steps)]
     host_out = torch.empty((B, T), dtype=torch.long).pin_memory()
     ttft, dec_ms, tot_ms = [], [], []
+    eager_launches = 0
     with ClockSampler(device.index) as clocks:
         for i, prompt in enumerate(prompts):
             _barrier(ws)
             torch.cuda.synchronize()
             e0, e1, e2 = (torch.cuda.Event(True) for _ in range(3))
+            n0 = N.kernel_launches()
             e0.record()
             dec.prefill(prompt)
             e1.record()
+            if i >= args.warmup:
+                eager_launches += N.kernel_launches() - n0
             ids = dec.decode(T - 1)
             e2.record()
             host_out.copy_(ids, non_blocking=True)
@@ -594,7 +623,8 @@ def run_generate(args, ws, rank, device):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_med, 3), "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "int8 + bf16 projections, bf16 elsewhere",
-        "data": "synthetic (random-init weights, uniform random tile maps and token ids)",
+        "data": "synthetic (random-init weights and token ids; tile maps " +
+                ("by IAA on the GPU over 64 x 2048 random ids)" if spec.get("calib") == "iaa" else "uniform random)"),
         "config": {"workload": f"config {'3' if args.model == 'llama3b' else ('4' if args.model == 'qwen7b' else '5')}:"
                                f" {args.model}", "layers": layers, "keep_bf16": spec["keep"], "batch": B,
                    "prompt": P, "new_tokens": T,
@@ -603,7 +633,8 @@ def run_generate(args, ws, rank, device):
         "ttft_ms_p50": round(statistics.median(ttft), 3), "tpot_ms_p50": round(d_med / (T - 1), 4),
         "e2e": {"value": round(jobs * B * T / (t_med * 1e-3), 1), "unit": "tokens/s (prefill + decode)",
                 "h2d_bytes_per_step": B * P * 8, "d2h_bytes_per_step": B * T * 8},
-        "gpu_launches": per_request * args.steps, "gpu_launches_per_graph": dec.captured_launches,
+        "gpu_launches": per_request * args.steps + eager_launches,
+        "gpu_launches_per_graph": dec.captured_launches, "prefill_captured": dec.prefill_captured,
         "clocks": clocks.summary(),
     }
 

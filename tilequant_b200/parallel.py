@@ -189,18 +189,28 @@ def shard_keep_ids(full_keep: torch.Tensor, full_shape: Tuple[int, int], shard: 
 
 
 def apply_sharded_tile_maps(model: nn.Module, shards: Dict[str, LinearShard], full_keep: Callable,
-                            full_shapes: Dict[str, Tuple[int, int]], cfg=None, model_type: str = "llama"):
+                            full_shapes: Dict[str, Tuple[int, int]], cfg=None, model_type: str = "llama",
+                            iaa_channel_stats: Optional[Dict[str, torch.Tensor]] = None):
     """Pack this rank's projection slices with the full model's tile maps restricted to
     them.  ``full_keep(name, n_tr, n_tc)`` gives the full projection's kept ids (the same
-    on every rank); ``full_shapes[name]`` its (out, in) features."""
+    on every rank); ``full_shapes[name]`` its (out, in) features; ``iaa_channel_stats``
+    the full projections' IAA channel means (sliced here to a row-parallel shard's input
+    columns)."""
     from .apply import apply_tile_maps
+
+    stats = None
+    if iaa_channel_stats is not None:
+        stats = {}
+        for name, sh in shards.items():
+            s = iaa_channel_stats[name]
+            stats[name] = s[sh.cols[0]:sh.cols[1]] if sh.cols is not None else s
 
     def keep_for(name: str, n_tr: int, n_tc: int) -> torch.Tensor:
         m, k = full_shapes[name]
         full = full_keep(name, (m + TILE - 1) // TILE, (k + TILE - 1) // TILE)
         return shard_keep_ids(torch.as_tensor(full), (m, k), shards[name])
 
-    return apply_tile_maps(model, keep_for, cfg, model_type=model_type, fuse_groups=True)
+    return apply_tile_maps(model, keep_for, cfg, model_type=model_type, iaa_channel_stats=stats, fuse_groups=True)
 
 
 def wrap_row_parallel_(model: nn.Module, shards: Dict[str, LinearShard], group=None) -> int:
@@ -223,13 +233,15 @@ def wrap_row_parallel_(model: nn.Module, shards: Dict[str, LinearShard], group=N
 
 
 def tensor_parallel_(model: nn.Module, rank: int, world: int, full_keep: Callable, cfg=None, group=None,
-                     model_type: str = "llama") -> Dict[str, LinearShard]:
+                     model_type: str = "llama",
+                     iaa_channel_stats: Optional[Dict[str, torch.Tensor]] = None) -> Dict[str, LinearShard]:
     """Shard, pack and wire a dense decoder for tensor parallelism in one call: the
     full model's tile maps ``full_keep(name, n_tr, n_tc)`` (identical on every rank)
     are restricted to this rank's slices."""
     shapes = projection_shapes(model)
     shards = shard_decoder_(model, rank, world)
-    apply_sharded_tile_maps(model, shards, full_keep, shapes, cfg, model_type=model_type)
+    apply_sharded_tile_maps(model, shards, full_keep, shapes, cfg, model_type=model_type,
+                            iaa_channel_stats=iaa_channel_stats)
     wrap_row_parallel_(model, shards, group)
     return shards
 
