@@ -4,7 +4,8 @@
  * Drop-in boundary for the reference's Triton path (HanzhiZhang-Ulrica/TileQuant,
  * src/kernels/triton/ and the torch paths of src/kernels/quant_utils.py and
  * src/kernels/pack.py).  Every entry point takes plain device pointers, element
- * strides and a cudaStream_t passed as void*; nothing here allocates device memory.
+ * strides and a cudaStream_t passed as void*; nothing here allocates device memory
+ * except tq_peer_alloc (the exchange buffer of the tensor-parallel peer sum).
  * All kernels are asynchronous on `stream` and may be captured in a CUDA graph.
  *
  * Return value: TQ_OK (0) or a TQ_ERR_* code; tq_last_error() gives a message for
@@ -164,6 +165,51 @@ TQ_API int tq_pack_int8_tiles(const void* w, int w_dtype, int64_t m, int64_t k, 
 /* Gather the 16-bit tiles `ids` unchanged (zero padded).  replaces pack.py:172-177. */
 TQ_API int tq_gather_fp_tiles(const void* w, int w_dtype, int64_t m, int64_t k, int64_t ldw, int n_tc,
                        const int32_t* ids, int64_t t16, void* tiles, void* stream);
+
+/* ---------------------------------------------------------------- tensor-parallel peer sum
+ * No counterpart in the reference, which runs on one GPU: for a row-parallel projection
+ * (K split across the ranks of one node, one process per GPU) the decode GEMM sums the
+ * ranks' partial outputs itself, over NVLink, instead of a separate all-reduce after
+ * it.  Each rank allocates one exchange buffer, exports it (tq_peer_ipc_handle), maps
+ * every peer's (tq_peer_ipc_open) and passes the device array of the world pointers
+ * (its own at index rank) plus its per-CTA call counters (uint32[slots], zeroed once). */
+
+#define TQ_PEER_MAX_WORLD 8
+#define TQ_PEER_MAX_SLOTS 65536
+#define TQ_IPC_HANDLE_BYTES 64
+
+/* Bytes of one exchange buffer for `world` ranks and `slots` CTA slots (0 if out of range). */
+TQ_API int64_t tq_peer_buffer_bytes(int world, int slots);
+
+/* cudaMalloc'd, zeroed exchange buffer on the current device; tq_peer_free releases it. */
+TQ_API int tq_peer_alloc(int world, int slots, void** buf);
+TQ_API int tq_peer_free(void* buf);
+
+/* The buffer's CUDA IPC handle (TQ_IPC_HANDLE_BYTES bytes) and its mapping in another
+ * process on another GPU of the node; tq_peer_ipc_close unmaps. */
+TQ_API int tq_peer_ipc_handle(void* buf, void* handle);
+TQ_API int tq_peer_ipc_open(const void* handle, void** buf);
+TQ_API int tq_peer_ipc_close(void* buf);
+
+/* Zero the buffer's flags and the counters (stream-ordered).  Every rank must reset
+ * before any rank's next peer-sum call, e.g. after a timeout. */
+TQ_API int tq_peer_reset(void* buf, int world, int slots, uint32_t* epochs, void* stream);
+
+/* tq_gemm_mixed on the decode kernel (1..16 rows, split_k 0..8) for this rank's K slice,
+ * with the world ranks' FP32 partials summed in rank order 0..world-1 inside the kernel
+ * before the output rounding and the bias: every rank gets the same (n_rows, m) output.
+ * Every rank must make the same sequence of calls (same n_rows, m, n_tr).  Needs
+ * 4 * n_tr <= slots and all 4 * n_tr CTAs resident at once (else TQ_ERR_UNSUPPORTED).
+ * A wait for a peer that exceeds timeout_ns writes TQ_ERR_TIMEOUT to `err` and the
+ * output is then undefined; reset the exchange on every rank before going on. */
+TQ_API int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
+                                  const float* int8_scales, const int32_t* int8_tile_ids,
+                                  const int32_t* int8_row_ptr, int64_t t8, const void* x_fp, int64_t ld_xfp,
+                                  const void* fp16_tiles, const int32_t* fp16_tile_ids,
+                                  const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype, void* out, int64_t ldo,
+                                  int out_dtype, const void* bias, int64_t n_rows, int64_t m, int64_t k, int n_tr,
+                                  int n_tc, int split_k, float* const* peer_bufs, uint32_t* epochs, int world,
+                                  int rank, int slots, int64_t timeout_ns, int* err, void* stream);
 
 /* ---------------------------------------------------------------- calibration */
 

@@ -1,6 +1,8 @@
 """Tensor parallelism on 2 GPUs (skipped with fewer): the sharded MixedLinear decoder
 against the unsharded one, eager forward and CUDA-graph greedy decoding with the NCCL
-all-reduces captured in the graphs."""
+all-reduces captured in the graphs -- or, with a PeerExchange, the decode-sized
+row-parallel sums done inside the decode GEMM over NVLink -- and a K-split GEMM
+through the peer sum against the unsplit GEMM."""
 
 from __future__ import annotations
 
@@ -35,7 +37,7 @@ def _model(dev, qwen=False):
         return Model(cfg).to(torch.bfloat16).eval()
 
 
-def _worker(rank, world, port, qwen, out_q):
+def _worker(rank, world, port, qwen, peer, out_q):
     import os
 
     import torch.distributed as dist
@@ -43,6 +45,7 @@ def _worker(rank, world, port, qwen, out_q):
     from tilequant_b200.apply import apply_tile_maps
     from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
     from tilequant_b200.parallel import projection_shapes, seeded_random_keep, tensor_parallel_
+    from tilequant_b200.peer import PeerExchange
 
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     dev = torch.device("cuda", rank)
@@ -51,7 +54,10 @@ def _worker(rank, world, port, qwen, out_q):
 
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120), device_id=dev)
+    exchange = None
     try:
+        if peer:
+            exchange = PeerExchange(dev, world, rank).connect()
         mtype = "qwen2" if qwen else "llama"
         full = _model(dev, qwen)
         keep = seeded_random_keep(0.1, 5, list(projection_shapes(full)))
@@ -61,7 +67,7 @@ def _worker(rank, world, port, qwen, out_q):
             want = full(input_ids=ids).logits.float()
         del full
         model = _model(dev, qwen)
-        tensor_parallel_(model, rank, world, keep, model_type=mtype)
+        tensor_parallel_(model, rank, world, keep, model_type=mtype, exchange=exchange)
         with torch.inference_mode():
             got = model(input_ids=ids).logits.float()
         rel = float((got - want).abs().max() / want.abs().max())
@@ -72,28 +78,127 @@ def _worker(rank, world, port, qwen, out_q):
         gathered = [torch.empty_like(toks) for _ in range(world)]
         dist.all_gather(gathered, toks)
         same = all(torch.equal(g, toks) for g in gathered)
-        out_q.put((rank, rel, agree, same))
+        status = 0 if exchange is None else exchange.status()
+        out_q.put((rank, rel, agree, same, status))
     finally:
+        if exchange is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            exchange.close()
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("qwen", [False, True])
-def test_tensor_parallel_two_gpus(qwen):
+@pytest.mark.parametrize("qwen,peer", [(False, False), (True, False), (False, True), (True, True)])
+def test_tensor_parallel_two_gpus(qwen, peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, qwen, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, qwen, peer, q)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in procs]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, rel, agree, same in res:
-        # row-parallel partials are rounded to BF16 before the sum, and the difference
-        # travels through every later layer in BF16
+    for rank, rel, agree, same, status in res:
+        # row-parallel partials are summed in another order than the single-GPU K loop
+        # (and rounded to BF16 first on the NCCL path), and the difference travels
+        # through every later layer in BF16
         assert rel < 5e-2, (rank, rel)
         assert agree > 0.9, (rank, agree)
         assert same, rank  # every rank generates the same tokens
+        assert status == 0, rank  # no peer wait ran out
+
+
+def _gemm_worker(rank, world, port, out_q):
+    import datetime
+    import os
+    from types import SimpleNamespace
+
+    import torch.distributed as dist
+
+    import tilequant_b200 as tq
+    from tilequant_b200.apply import complement_ids
+    from tilequant_b200.parallel import restrict_keep_ids
+    from tilequant_b200.peer import PeerExchange, gemm_mixed_peer_sum
+    from tests.golden import inputs as I
+    from tests.helpers import assert_close_gemm, assert_close_with_bias, from_torch16
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    exchange = PeerExchange(dev, world, rank).connect()
+    try:
+        cfg = SimpleNamespace(tile_m=64, tile_n=64, pad_to_tile=True, quant_style="gi")
+        m, k = 2048, 4096
+        n_tr, n_tc = m // 64, k // 64
+        w = I.weight(m, k, 40).to(dev)
+        keep = I.keep_ids(n_tr, n_tc, 0.05, 41)
+        full = tq.pack_weight_from_tile_ids(w, n_tr=n_tr, n_tc=n_tc, int8_tile_ids=complement_ids(keep, n_tr * n_tc),
+                                            fp16_tile_ids=keep, cfg=cfg)
+        c0, c1 = rank * n_tc // world, (rank + 1) * n_tc // world
+        kk, _, _ = restrict_keep_ids(keep, n_tc, rows=(0, n_tr), cols=(c0, c1))
+        part = tq.pack_weight_from_tile_ids(w[:, c0 * 64:c1 * 64].contiguous(), n_tr=n_tr, n_tc=c1 - c0,
+                                            int8_tile_ids=complement_ids(kk, n_tr * (c1 - c0)), fp16_tile_ids=kk,
+                                            cfg=cfg)
+
+        def wts(p):
+            return dict(int8_tiles=p.int8_tiles, int8_scales=p.int8_scales, int8_tile_ids=p.int8_tile_ids,
+                        int8_row_ptr=p.int8_row_ptr, fp16_tiles=p.fp16_tiles, fp16_tile_ids=p.fp16_tile_ids,
+                        fp16_row_ptr=p.fp16_row_ptr, M=p.M_orig, K=p.K_orig, n_tr=p.n_tr, n_tc=p.n_tc)
+
+        bias_all = (torch.randn(m, generator=I.gen(42)) * 0.5).to(dev, torch.bfloat16)
+        errors = []
+        same = True
+        for rows in (1, 7, 16):
+            for call in range(2):
+                bias = bias_all if call else None
+                x = I.activations(rows, k, 50 + 10 * rows + call).to(dev)
+                q, sx = tq.quantize_activation_tile_absmax(x)
+                want = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, out_dtype=torch.bfloat16, bias=bias,
+                                                 **wts(full))
+                xs = x[:, c0 * 64:c1 * 64].contiguous()
+                qs, ss = tq.quantize_activation_tile_absmax(xs)
+                got = gemm_mixed_peer_sum(x_fp=xs, x_int8=qs, sx=ss, out_dtype=torch.bfloat16, bias=bias,
+                                          exchange=exchange, **wts(part))
+                torch.cuda.synchronize()
+                try:  # FP32 partial sums in another association than the unsplit K loop
+                    if bias is None:
+                        assert_close_gemm(from_torch16(got), from_torch16(want), f"rows {rows}")
+                    else:
+                        assert_close_with_bias(from_torch16(got), from_torch16(want), from_torch16(bias),
+                                               f"rows {rows} + bias")
+                except AssertionError as e:
+                    errors.append(str(e))
+                gathered = [torch.empty_like(got) for _ in range(world)]
+                dist.all_gather(gathered, got)
+                same = same and all(torch.equal(g.view(torch.int16), got.view(torch.int16)) for g in gathered)
+        out_q.put((rank, errors, same, exchange.status()))
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        exchange.close()
+        dist.destroy_process_group()
+
+
+def test_peer_sum_gemm_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gemm_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, errors, same, status in res:
+        assert status == 0, rank
+        assert same, rank  # the same bits on every rank
+        assert not errors, (rank, errors)

@@ -71,6 +71,25 @@ def test_host_side_argument_checks(lib):
     assert lib.tq_calib_iaa_tile_scores(dummy, 0, 64, 64, 64, dummy, 0, dummy, dummy, None) == N.TQ_ERR_INVALID
 
 
+def test_peer_sum_host_side_checks(lib):
+    # exchange layout: u32 flags [world][slots] padded to 256 B, then f32 [2][world][slots][256]
+    assert lib.tq_peer_buffer_bytes(2, 1024) == 8192 + 2 * 2 * 1024 * 256 * 4
+    assert lib.tq_peer_buffer_bytes(3, 5) == 256 + 2 * 3 * 5 * 256 * 4
+    assert lib.tq_peer_buffer_bytes(0, 16) == 0 and lib.tq_peer_buffer_bytes(9, 16) == 0
+    assert lib.tq_peer_buffer_bytes(2, 0) == 0 and lib.tq_peer_buffer_bytes(2, 65537) == 0
+    out = ctypes.c_void_p()
+    assert lib.tq_peer_alloc(0, 16, ctypes.byref(out)) == N.TQ_ERR_INVALID and out.value is None
+    assert lib.tq_peer_reset(None, 2, 16, None, None) == N.TQ_ERR_INVALID
+    dummy = ctypes.c_void_p(16)
+    args = [dummy, 64, dummy, dummy, dummy, dummy, dummy, 1, None, 64, None, None, None, 0, 0, dummy, 64, 0, None,
+            1, 64, 64, 1, 1, 0]
+    for world, rank, slots, timeout in [(9, 0, 16, 10**9), (2, 2, 16, 10**9), (2, 0, 0, 10**9), (2, 0, 16, 0)]:
+        rc = lib.tq_gemm_mixed_peer_sum(*args, dummy, dummy, world, rank, slots, timeout, None, None)
+        assert rc == N.TQ_ERR_INVALID, (world, rank, slots, timeout)
+    rc = lib.tq_gemm_mixed_peer_sum(*args, None, dummy, 2, 0, 16, 10**9, None, None)
+    assert rc == N.TQ_ERR_INVALID and b"exchange" in lib.tq_last_error()
+
+
 def test_python_errors_map_to_reference_exceptions(lib):
     with pytest.raises(ValueError):
         N.check(N.TQ_ERR_INVALID, "x")

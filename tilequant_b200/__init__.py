@@ -15,6 +15,7 @@ from .mixed_linear import (
     reset_projection_groups,
 )
 from .pack import Pack, concat_packs_along_rows, is_row_major_pack, pack_weight, pack_weight_from_tile_ids
+from .peer import PeerExchange, gemm_mixed_peer_sum
 from .quant_utils import (
     activation_tile_absmax_scales,
     pad_to_multiple,
@@ -23,9 +24,9 @@ from .quant_utils import (
 )
 
 __all__ = [
-    "MixedLinear", "MixedLinearGroup", "MixedLinearSlice", "Pack", "activation_tile_absmax_scales",
+    "MixedLinear", "MixedLinearGroup", "MixedLinearSlice", "Pack", "PeerExchange", "activation_tile_absmax_scales",
     "concat_packs_along_rows", "fuse_projection_groups", "gemm_int8_partials", "gemm_mixed_fused_quant",
-    "gemm_mixed_rows_splitk", "is_row_major_pack", "pack_weight", "pack_weight_from_tile_ids", "pad_to_multiple",
-    "quantize_activation_tile_absmax", "quantize_activation_tile_with_scales", "reset_projection_groups",
-    "select_split_k",
+    "gemm_mixed_peer_sum", "gemm_mixed_rows_splitk", "is_row_major_pack", "pack_weight",
+    "pack_weight_from_tile_ids", "pad_to_multiple", "quantize_activation_tile_absmax",
+    "quantize_activation_tile_with_scales", "reset_projection_groups", "select_split_k",
 ]

@@ -42,7 +42,18 @@ SIGNATURES = {
     "tq_calib_gi_accumulate": [_P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _P],
     "tq_calib_iaa_channel_accumulate": [_P, _I, _I64, _I64, _I64, _P, _P],
     "tq_calib_iaa_tile_scores": [_P, _I, _I64, _I64, _I64, _P, _I64, _P, _P, _P],
+    "tq_peer_buffer_bytes": [_I, _I],
+    "tq_peer_alloc": [_I, _I, _P],
+    "tq_peer_free": [_P],
+    "tq_peer_ipc_handle": [_P, _P],
+    "tq_peer_ipc_open": [_P, _P],
+    "tq_peer_ipc_close": [_P],
+    "tq_peer_reset": [_P, _I, _I, _P, _P],
+    "tq_gemm_mixed_peer_sum": [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I, _P, _I64, _I, _P,
+                               _I64, _I64, _I64, _I, _I, _I, _P, _P, _I, _I, _I, _I64, _P, _P],
 }
+
+TQ_PEER_MAX_WORLD, TQ_PEER_MAX_SLOTS, TQ_IPC_HANDLE_BYTES = 8, 65536, 64
 
 _lib = None
 _lock = threading.Lock()
@@ -71,6 +82,7 @@ def load() -> ctypes.CDLL:
             lib.tq_last_error.restype = ctypes.c_char_p
             lib.tq_status_string.restype = ctypes.c_char_p
             lib.tq_kernel_launches.restype = ctypes.c_int64
+            lib.tq_peer_buffer_bytes.restype = ctypes.c_int64
             if lib.tq_abi_version() != ABI_VERSION:
                 raise TileQuantError("libtilequant_b200.so ABI version mismatch; rebuild it")
             _lib = lib

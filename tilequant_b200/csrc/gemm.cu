@@ -29,25 +29,24 @@ static int check_pack(const int8_t* w8, const float* s8, const int32_t* ids8, co
   return TQ_OK;
 }
 
-extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
-                             const float* int8_scales, const int32_t* int8_tile_ids, const int32_t* int8_row_ptr,
-                             int64_t t8, const void* x_fp, int64_t ld_xfp, const void* fp16_tiles,
-                             const int32_t* fp16_tile_ids, const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype,
-                             void* out, int64_t ldo, int out_dtype, const void* bias, int64_t n_rows, int64_t m,
-                             int64_t k, int n_tr, int n_tc, int split_k, int algo, int* err, void* stream) {
+// Validates the operands of a mixed GEMM and fills the kernel arguments.
+static int gemm_args(tq::RowsArgs& a, const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
+                     const float* int8_scales, const int32_t* int8_tile_ids, const int32_t* int8_row_ptr, int64_t t8,
+                     const void* x_fp, int64_t ld_xfp, const void* fp16_tiles, const int32_t* fp16_tile_ids,
+                     const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype, void* out, int64_t ldo, int out_dtype,
+                     const void* bias, int64_t n_rows, int64_t m, int64_t k, int n_tr, int n_tc, int split_k, int* err) {
   int rc = check_pack(int8_tiles, int8_scales, int8_tile_ids, int8_row_ptr, t8, fp16_tiles, fp16_tile_ids,
                       fp16_row_ptr, t16, m, k, n_tr, n_tc);
   if (rc) return rc;
   if (fp_dtype != TQ_DTYPE_BF16 && fp_dtype != TQ_DTYPE_F16) return tq_set_error(TQ_ERR_INVALID, "bad fp dtype");
   if (out_dtype != TQ_DTYPE_BF16 && out_dtype != TQ_DTYPE_F16) return tq_set_error(TQ_ERR_INVALID, "bad out dtype");
   if (n_rows < 0) return tq_set_error(TQ_ERR_INVALID, "negative n_rows");
-  if (n_rows == 0) return TQ_OK;
   if (n_rows > INT32_MAX / 2) return tq_set_error(TQ_ERR_INVALID, "n_rows too large");
-  if (!out || ldo < m) return tq_set_error(TQ_ERR_INVALID, "out must be (n_rows, m) with row stride >= m");
-  if (t8 > 0 && (!x_i8 || !sx || ld_x8 < k)) return tq_set_error(TQ_ERR_INVALID, "x_int8 must be (n_rows, k)");
-  if (t16 > 0 && (!x_fp || ld_xfp < k)) return tq_set_error(TQ_ERR_INVALID, "x_fp must be (n_rows, k)");
+  if (n_rows > 0 && (!out || ldo < m)) return tq_set_error(TQ_ERR_INVALID, "out must be (n_rows, m) with row stride >= m");
+  if (n_rows > 0 && t8 > 0 && (!x_i8 || !sx || ld_x8 < k)) return tq_set_error(TQ_ERR_INVALID, "x_int8 must be (n_rows, k)");
+  if (n_rows > 0 && t16 > 0 && (!x_fp || ld_xfp < k)) return tq_set_error(TQ_ERR_INVALID, "x_fp must be (n_rows, k)");
   if (split_k < 0 || split_k > 16) return tq_set_error(TQ_ERR_INVALID, "split_k must be 0 (auto) or 1..16");
-  tq::RowsArgs a = {};
+  a = tq::RowsArgs{};
   a.x_i8 = x_i8;
   a.ld_x8 = ld_x8;
   a.sx = sx;
@@ -73,6 +72,21 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
   a.has_fp16 = t16 > 0;
   a.w8_rows = t8 * 64;
   a.w16_rows = t16 * 64;
+  return TQ_OK;
+}
+
+extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
+                             const float* int8_scales, const int32_t* int8_tile_ids, const int32_t* int8_row_ptr,
+                             int64_t t8, const void* x_fp, int64_t ld_xfp, const void* fp16_tiles,
+                             const int32_t* fp16_tile_ids, const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype,
+                             void* out, int64_t ldo, int out_dtype, const void* bias, int64_t n_rows, int64_t m,
+                             int64_t k, int n_tr, int n_tc, int split_k, int algo, int* err, void* stream) {
+  tq::RowsArgs a;
+  int rc = gemm_args(a, x_i8, ld_x8, sx, int8_tiles, int8_scales, int8_tile_ids, int8_row_ptr, t8, x_fp, ld_xfp,
+                     fp16_tiles, fp16_tile_ids, fp16_row_ptr, t16, fp_dtype, out, ldo, out_dtype, bias, n_rows, m, k,
+                     n_tr, n_tc, split_k, err);
+  if (rc) return rc;
+  if (n_rows == 0) return TQ_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (algo == TQ_ALGO_UMMA || (algo == TQ_ALGO_AUTO && n_rows > 64 && t8 > 0 &&
                                tq_umma_supported(n_rows, m, k, x_i8, ld_x8, x_fp, ld_xfp, int8_tiles, fp16_tiles))) {
@@ -86,6 +100,34 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
   }
   if (algo != TQ_ALGO_AUTO && algo != TQ_ALGO_ROWS) return tq_set_error(TQ_ERR_INVALID, "unknown algo");
   return tq_launch_rows(a, n_tr, fp_dtype, st, t16);
+}
+
+extern "C" int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,
+                                      const float* int8_scales, const int32_t* int8_tile_ids,
+                                      const int32_t* int8_row_ptr, int64_t t8, const void* x_fp, int64_t ld_xfp,
+                                      const void* fp16_tiles, const int32_t* fp16_tile_ids,
+                                      const int32_t* fp16_row_ptr, int64_t t16, int fp_dtype, void* out, int64_t ldo,
+                                      int out_dtype, const void* bias, int64_t n_rows, int64_t m, int64_t k, int n_tr,
+                                      int n_tc, int split_k, float* const* peer_bufs, uint32_t* epochs, int world,
+                                      int rank, int slots, int64_t timeout_ns, int* err, void* stream) {
+  tq::RowsArgs a;
+  int rc = gemm_args(a, x_i8, ld_x8, sx, int8_tiles, int8_scales, int8_tile_ids, int8_row_ptr, t8, x_fp, ld_xfp,
+                     fp16_tiles, fp16_tile_ids, fp16_row_ptr, t16, fp_dtype, out, ldo, out_dtype, bias, n_rows, m, k,
+                     n_tr, n_tc, split_k, err);
+  if (rc) return rc;
+  if (world < 1 || world > TQ_PEER_MAX_WORLD || rank < 0 || rank >= world)
+    return tq_set_error(TQ_ERR_INVALID, "peer sum: need 1 <= world <= 8 and 0 <= rank < world");
+  if (!peer_bufs || !epochs || slots < 1 || timeout_ns <= 0)
+    return tq_set_error(TQ_ERR_INVALID, "peer sum: exchange buffers, counters, slots and timeout are required");
+  if (n_rows == 0) return TQ_OK;  // every rank sees the same n_rows, so all skip together
+  if (!tq_gemv_supported(a)) return tq_set_error(TQ_ERR_UNSUPPORTED, "peer sum: needs 1..16 rows and split_k <= 8");
+  a.peer_bufs = peer_bufs;
+  a.peer_epochs = epochs;
+  a.world = world;
+  a.rank = rank;
+  a.peer_slots = slots;
+  a.peer_timeout_ns = timeout_ns;
+  return tq_launch_gemv(a, n_tr, fp_dtype, (cudaStream_t)stream);
 }
 
 extern "C" int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dtype, const int8_t* int8_tiles,

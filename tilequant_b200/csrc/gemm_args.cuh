@@ -34,6 +34,22 @@ struct RowsArgs {
   int afp_vec;         // x_fp rows are 16-byte addressable
   int fused;           // quantize x_fp in the kernel (x_i8 / sx unused)
   int tma_x;           // activation tensor maps are valid (set by the launcher)
+  // Row-parallel peer sum (decode kernel only; world 0 = off): CTA b of every rank
+  // writes its FP32 partial tile into slot b of every rank's exchange buffer, then sums
+  // the world partials found in its own buffer in rank order.
+  float* const* peer_bufs;  // device array [world] of the exchange buffers, mapped on this GPU
+  uint32_t* peer_epochs;    // this rank's per-CTA call counters [peer_slots]
+  int world, rank, peer_slots;
+  int64_t peer_timeout_ns;  // bound of every wait for a peer's partial
 };
+
+// Exchange buffer of the peer sum: flags u32 [world][slots] (padded to 256 bytes), then
+// partials f32 [2 (call parity)][world (source rank)][slots][256 (16 rows x 16 columns)].
+__host__ __device__ inline int64_t peer_flag_bytes(int world, int slots) {
+  return (((int64_t)world * slots * 4 + 255) / 256) * 256;
+}
+__host__ __device__ inline int64_t peer_buffer_bytes(int world, int slots) {
+  return peer_flag_bytes(world, slots) + (int64_t)2 * world * slots * 256 * 4;
+}
 
 }  // namespace tq

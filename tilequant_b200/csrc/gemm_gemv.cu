@@ -26,6 +26,19 @@
 // Quantization stays a separate launch: quantizing inside this kernel repeats it in
 // every CTA (n_tr * 4 times per column tile), which cost more than the launch saved.
 // The results are bit-identical to the split-K row kernel at the same split.
+//
+// Row-parallel peer sum (PEER): for a tensor-parallel projection split along K, the
+// partial outputs of the ranks are summed inside this kernel instead of by a separate
+// all-reduce.  CTA b writes its FP32 partial (16 rows x 16 columns) into slot b of every
+// rank's exchange buffer with plain stores over NVLink (the buffers are CUDA IPC
+// mappings), publishes it with a system-scope release flag holding its call number,
+// waits (bounded by a timeout that sets an error word, never forever) until every rank's
+// flag for slot b reaches that number, then adds the partials of ranks 0..world-1 in
+// that order, rounds and adds the bias -- the same bits on every rank.  Partials
+// alternate between two buffers by call parity: a rank can only write call e + 2 after
+// finishing call e + 1, which needed every rank's call e + 1 partial, so every rank has
+// read its call e partials by then.  All CTAs of the grid must be resident at once
+// (the launcher checks), so a waiting CTA never holds the SM a peer's partial needs.
 #include "common.cuh"
 #include "gemm_args.cuh"
 #include "tma.cuh"
@@ -47,6 +60,20 @@ __device__ __forceinline__ uint4 ldg16_row(const uint8_t* row, int off, int len,
   uint32_t w[4] = {0u, 0u, 0u, 0u};
   for (int e = 0; e < 16 && off + e < len; ++e) w[e >> 2] |= (uint32_t)row[off + e] << ((e & 3) * 8);
   return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ float i2f_exact_gv(int v) {
@@ -113,7 +140,7 @@ __device__ __forceinline__ void run_chunk(const RowsArgs& a, const WChunk<N>& c,
   }
 }
 
-template <int XT>
+template <int XT, bool PEER>
 __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs a) {
   constexpr int UC = 6;  // INT8 tiles per chunk
 
@@ -182,10 +209,61 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
 #pragma unroll
     for (int q = 0; q < 4; ++q) mine[(g + 8 * (q >> 1)) * 16 + nb * 8 + 2 * t + (q & 1)] = acc[nb][q];
   __syncthreads();
+  const float* sum_src = nullptr;  // PEER: this CTA's slot of ranks 0.. in the own buffer
+  int64_t sum_stride = 0;
+  if constexpr (PEER) {
+    __shared__ __align__(16) float red[256];
+    __shared__ uint32_t s_ep;
+    for (int e = tid; e < 256; e += blockDim.x) {
+      float v = part[e];
+      for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
+      red[e] = v;
+    }
+    const int b = blockIdx.x, W = a.world, slots = a.peer_slots;
+    if (tid == 0) {  // only this CTA of this rank touches its counter; launches are stream-ordered
+      const uint32_t ep = a.peer_epochs[b] + 1u;
+      a.peer_epochs[b] = ep;
+      s_ep = ep;
+    }
+    __syncthreads();
+    const uint32_t ep = s_ep;
+    const int64_t flag_floats = peer_flag_bytes(W, slots) / 4;
+    const int64_t par_base = flag_floats + (int64_t)(ep & 1u) * W * slots * 256;
+    for (int i = tid; i < 64 * W; i += blockDim.x) {
+      float* dst = a.peer_bufs[i >> 6] + par_base + ((int64_t)a.rank * slots + b) * 256;
+      reinterpret_cast<float4*>(dst)[i & 63] = reinterpret_cast<const float4*>(red)[i & 63];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid < W) st_release_sys(reinterpret_cast<uint32_t*>(a.peer_bufs[tid]) + (int64_t)a.rank * slots + b, ep);
+    float* own = a.peer_bufs[a.rank];
+    if (tid < W) {  // thread p waits for rank p's partial of this slot
+      const uint32_t* f = reinterpret_cast<const uint32_t*>(own) + (int64_t)tid * slots + b;
+      const uint64_t t0 = globaltimer_ns();
+      unsigned ns = 32;
+      while ((int32_t)(ld_acquire_sys(f) - ep) < 0) {
+        if ((int64_t)(globaltimer_ns() - t0) > a.peer_timeout_ns) {
+          report(a.err, TQ_ERR_TIMEOUT);
+          break;
+        }
+        __nanosleep(ns);
+        if (ns < 1024) ns <<= 1;
+      }
+    }
+    __syncthreads();
+    sum_src = own + par_base + b * 256;
+    sum_stride = (int64_t)slots * 256;
+  }
   for (int e = tid; e < 256; e += blockDim.x) {
     const int j = e >> 4, tok = e & 15;
-    float v = part[e];
-    for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
+    float v;
+    if constexpr (PEER) {
+      v = __ldcv(sum_src + e);  // not cached: written by other GPUs
+      for (int p = 1; p < a.world; ++p) v += __ldcv(sum_src + p * sum_stride + e);  // rank order
+    } else {
+      v = part[e];
+      for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
+    }
     const int cc = r * 64 + 16 * m + j;
     if (tok < a.n_rows && cc < a.M && a.out) {
       const int ot = a.out_dtype;
@@ -212,6 +290,18 @@ int tq_gemv_supported(const RowsArgs& a) {
   return a.n_rows > 0 && a.n_rows <= 16 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
 }
 
+template <int XT, bool PEER>
+static int launch_gemv_t(const RowsArgs& a, const cudaLaunchConfig_t& cfg) {
+  if (PEER) {  // a waiting CTA must never hold the SM a later CTA of its grid needs
+    int per_sm = 0;
+    TQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<XT, PEER>, cfg.blockDim.x, 0));
+    if ((int64_t)per_sm * tq_sm_count() < (int64_t)cfg.gridDim.x)
+      return tq_set_error(TQ_ERR_UNSUPPORTED, "peer sum: the decode grid does not fit on the GPU at once");
+  }
+  TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<XT, PEER>, a));
+  return TQ_OK;
+}
+
 int tq_launch_gemv(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st) {
   a.n_tr = n_tr;
   a.a8_vec = a.x_i8 && ((uintptr_t)a.x_i8 & 15) == 0 && (a.ld_x8 & 15) == 0;
@@ -233,11 +323,15 @@ int tq_launch_gemv(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  if (fp_dtype == TQ_DTYPE_BF16) {
-    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<TQ_DTYPE_BF16>, a));
-  } else {
-    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<TQ_DTYPE_F16>, a));
-  }
+  if (a.world > 0 && (int64_t)n_tr * 4 > a.peer_slots)
+    return tq_set_error(TQ_ERR_INVALID, "peer sum: more decode CTAs than exchange slots");
+  const bool peer = a.world > 0;
+  int rc;
+  if (fp_dtype == TQ_DTYPE_BF16)
+    rc = peer ? launch_gemv_t<TQ_DTYPE_BF16, true>(a, cfg) : launch_gemv_t<TQ_DTYPE_BF16, false>(a, cfg);
+  else
+    rc = peer ? launch_gemv_t<TQ_DTYPE_F16, true>(a, cfg) : launch_gemv_t<TQ_DTYPE_F16, false>(a, cfg);
+  if (rc != TQ_OK) return rc;
   tq_count_launch();
   return TQ_OK;
 }

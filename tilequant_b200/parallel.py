@@ -11,7 +11,9 @@ columns):
   tiles (attention: the columns of its own heads), packs only those tiles with their
   unchanged per-tile scales, quantizes only those activation columns (the same codes
   and scales the full GEMM computes for them), and the partial outputs are summed
-  with one NCCL all-reduce per layer; a bias is added once, after the sum.
+  with one NCCL all-reduce per layer; a bias is added once, after the sum.  With a
+  ``PeerExchange`` (``peer.py``), decode-sized calls (1..16 rows) sum the partials
+  inside the decode GEMM instead, over NVLink, in FP32 and in rank order.
 
 Attention heads: rank r of t owns query heads [q0, q1) and the KV heads they read.
 When there are fewer KV heads than ranks (Qwen2.5-7B: 4 KV heads at TP 8), each KV
@@ -95,6 +97,47 @@ def _slice_linear(lin: nn.Linear, rows: Optional[Tuple[int, int]] = None,
             b = lin.bias.detach()
             out.bias.copy_(b[rows[0]:rows[1]] if rows is not None else b)
     return out
+
+
+class PeerReduceSum(nn.Module):
+    """Row-parallel ``MixedLinear`` whose decode-sized calls (1..16 rows) sum the ranks'
+    partials inside the GEMM through a ``PeerExchange``; larger calls take the NCCL
+    all-reduce of ``AllReduceSum``.  The bias is added once, after the sum, either way.
+    Every rank sees the same row counts, so all ranks take the same path."""
+
+    MAX_ROWS = 16
+
+    def __init__(self, inner: nn.Module, exchange, group=None, bias: Optional[torch.Tensor] = None):
+        super().__init__()
+        self.inner = inner
+        self.exchange = exchange
+        self.group = group
+        self.bias = None if bias is None else nn.Parameter(bias.detach().clone(), requires_grad=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        from .peer import gemm_mixed_peer_sum
+        from .quant_utils import quantize_activation_tile_absmax
+
+        inner = self.inner
+        rows = x.numel() // max(1, x.shape[-1])
+        if 0 < rows <= self.MAX_ROWS and x.dim() in (2, 3):
+            x2d = x.reshape(-1, x.shape[-1]).contiguous()
+            if x2d.shape[1] != inner.K_orig:
+                raise ValueError(f"Input K mismatch: got {x2d.shape[1]}, expected {inner.K_orig}")
+            out_dtype = inner._out_dtype()
+            bias = None if self.bias is None else self.bias.to(dtype=out_dtype).contiguous()
+            x_int8, sx = quantize_activation_tile_absmax(x2d, tile_n=inner.tile_n)
+            y = gemm_mixed_peer_sum(x_fp=x2d, x_int8=x_int8, sx=sx, out_dtype=out_dtype, exchange=self.exchange,
+                                    bias=bias, **inner._weights())
+            return y.reshape(*x.shape[:-1], inner.M_orig)
+        y = inner(x)
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.all_reduce(y, group=self.group)
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y
 
 
 class AllReduceSum(nn.Module):
@@ -213,9 +256,12 @@ def apply_sharded_tile_maps(model: nn.Module, shards: Dict[str, LinearShard], fu
     return apply_tile_maps(model, keep_for, cfg, model_type=model_type, iaa_channel_stats=stats, fuse_groups=True)
 
 
-def wrap_row_parallel_(model: nn.Module, shards: Dict[str, LinearShard], group=None) -> int:
+def wrap_row_parallel_(model: nn.Module, shards: Dict[str, LinearShard], group=None, exchange=None) -> int:
     """Wrap every row-parallel projection (whatever module now holds it) in
-    ``AllReduceSum``; returns how many were wrapped."""
+    ``AllReduceSum``, or in ``PeerReduceSum`` when a ``PeerExchange`` is given and the
+    projection is a ``MixedLinear``; returns how many were wrapped."""
+    from .mixed_linear import MixedLinear
+
     modules = dict(model.named_modules())
     n = 0
     for name, sh in shards.items():
@@ -224,25 +270,30 @@ def wrap_row_parallel_(model: nn.Module, shards: Dict[str, LinearShard], group=N
         parent_name, _, attr = name.rpartition(".")
         parent = modules[parent_name] if parent_name else model
         inner = getattr(parent, attr)
-        if isinstance(inner, AllReduceSum):
+        if isinstance(inner, (AllReduceSum, PeerReduceSum)):
             continue
         bias = None if sh.bias is None else sh.bias.to(next(inner.buffers(), sh.bias).device)
-        setattr(parent, attr, AllReduceSum(inner, group, bias))
+        if exchange is not None and isinstance(inner, MixedLinear):
+            setattr(parent, attr, PeerReduceSum(inner, exchange, group, bias))
+        else:
+            setattr(parent, attr, AllReduceSum(inner, group, bias))
         n += 1
     return n
 
 
 def tensor_parallel_(model: nn.Module, rank: int, world: int, full_keep: Callable, cfg=None, group=None,
                      model_type: str = "llama",
-                     iaa_channel_stats: Optional[Dict[str, torch.Tensor]] = None) -> Dict[str, LinearShard]:
+                     iaa_channel_stats: Optional[Dict[str, torch.Tensor]] = None,
+                     exchange=None) -> Dict[str, LinearShard]:
     """Shard, pack and wire a dense decoder for tensor parallelism in one call: the
     full model's tile maps ``full_keep(name, n_tr, n_tc)`` (identical on every rank)
-    are restricted to this rank's slices."""
+    are restricted to this rank's slices.  ``exchange`` (a connected ``PeerExchange``)
+    moves the decode-sized row-parallel sums into the GEMM."""
     shapes = projection_shapes(model)
     shards = shard_decoder_(model, rank, world)
     apply_sharded_tile_maps(model, shards, full_keep, shapes, cfg, model_type=model_type,
                             iaa_channel_stats=iaa_channel_stats)
-    wrap_row_parallel_(model, shards, group)
+    wrap_row_parallel_(model, shards, group, exchange)
     return shards
 
 
