@@ -521,11 +521,12 @@ GEN_MODELS = {
 }
 
 
-def build_generation_model(spec, device, seed=0, tp=None):
+def build_generation_model(spec, device, seed=0, tp=None, exchange=None):
     """Random-init decoder of the given architecture on `device` (bf16), projections
     replaced by MixedLinear with uniformly random tile maps; with tp = (rank, world,
     group), this rank's tensor-parallel shard of it (the same full model and maps on
-    every rank)."""
+    every rank), its decode-sized row-parallel sums in the GEMM when `exchange` (a
+    connected PeerExchange) is given."""
     from tilequant_b200.apply import apply_random_tile_maps
     from tilequant_b200.parallel import projection_shapes, seeded_random_keep, tensor_parallel_
 
@@ -561,12 +562,12 @@ def build_generation_model(spec, device, seed=0, tp=None):
             apply_tile_maps(model, kept, cfg, model_type=spec["arch"], iaa_channel_stats=stats)
         else:
             tensor_parallel_(model, tp[0], tp[1], lambda n, n_tr, n_tc: kept[n], cfg, group=tp[2],
-                             model_type=spec["arch"], iaa_channel_stats=stats)
+                             model_type=spec["arch"], iaa_channel_stats=stats, exchange=exchange)
     elif tp is None:
         apply_random_tile_maps(model, spec["keep"], seed=seed + 1, model_type=spec["arch"])
     else:
         keep = seeded_random_keep(spec["keep"], seed + 1, list(projection_shapes(model)))
-        tensor_parallel_(model, tp[0], tp[1], keep, group=tp[2], model_type=spec["arch"])
+        tensor_parallel_(model, tp[0], tp[1], keep, group=tp[2], model_type=spec["arch"], exchange=exchange)
     torch.cuda.empty_cache()
     return model
 
@@ -578,7 +579,12 @@ def run_generate(args, ws, rank, device):
 
     spec = dict(GEN_MODELS[args.model])
     tp = args.tp and ws > 1
-    model = build_generation_model(spec, device, tp=(rank, ws, None) if tp else None)
+    exchange = None
+    if tp and args.allreduce == "peer":
+        from tilequant_b200.peer import PeerExchange
+
+        exchange = PeerExchange(device, ws, rank).connect()
+    model = build_generation_model(spec, device, tp=(rank, ws, None) if tp else None, exchange=exchange)
     B, P, T = spec["batch"], spec["prompt"], spec["new"]
     from tilequant_b200 import _native as N
 
@@ -612,6 +618,11 @@ def run_generate(args, ws, rank, device):
                 dec_ms.append(e1.elapsed_time(e2))
                 tot_ms.append(e0.elapsed_time(e2))
     dec.close()
+    peer_status = None
+    if exchange is not None:  # every rank takes the same collective steps, whatever its status
+        peer_status = int(_max_over_ranks(float(exchange.status()), ws))
+        _barrier(ws)
+        exchange.close()
     t_med = statistics.median(tot_ms)
     d_med = _max_over_ranks(statistics.median(dec_ms), ws)
     t_med = _max_over_ranks(t_med, ws)
@@ -628,13 +639,16 @@ def run_generate(args, ws, rank, device):
         "config": {"workload": f"config {'3' if args.model == 'llama3b' else ('4' if args.model == 'qwen7b' else '5')}:"
                                f" {args.model}", "layers": layers, "keep_bf16": spec["keep"], "batch": B,
                    "prompt": P, "new_tokens": T,
-                   "parallelism": f"tp{ws} (NCCL all-reduce after O and down)" if tp else f"replicas x{ws}",
+                   "parallelism": (f"tp{ws} (" + ("O/down sums inside the decode GEMM over NVLink for <= 16 rows, "
+                                                  "NCCL all-reduce otherwise)" if exchange is not None else
+                                                  "NCCL all-reduce after O and down)")) if tp else f"replicas x{ws}",
                    "l2": "weights (GBs) and KV cache exceed L2 every step"},
         "ttft_ms_p50": round(statistics.median(ttft), 3), "tpot_ms_p50": round(d_med / (T - 1), 4),
         "e2e": {"value": round(jobs * B * T / (t_med * 1e-3), 1), "unit": "tokens/s (prefill + decode)",
                 "h2d_bytes_per_step": B * P * 8, "d2h_bytes_per_step": B * T * 8},
         "gpu_launches": per_request * args.steps + eager_launches,
         "gpu_launches_per_graph": dec.captured_launches, "prefill_captured": dec.prefill_captured,
+        **({} if peer_status is None else {"peer_sum_status": peer_status}),
         "clocks": clocks.summary(),
     }
 
@@ -679,6 +693,8 @@ def main():
     ap.add_argument("--workload", choices=["prefill", "decode", "gemm", "generate"], default="prefill")
     ap.add_argument("--model", choices=sorted(GEN_MODELS), default="llama3b", help="model of --workload generate")
     ap.add_argument("--tp", action="store_true", help="--workload generate: tensor parallel over the ranks")
+    ap.add_argument("--allreduce", choices=["peer", "nccl"], default="peer",
+                    help="--tp: row-parallel sums of decode calls inside the GEMM (peer) or by NCCL")
     ap.add_argument("--shape", default="8192x16384x3072", help="ROWSxMxK of --workload gemm")
     ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
     ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")

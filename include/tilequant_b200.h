@@ -191,8 +191,8 @@ TQ_API int tq_peer_ipc_handle(void* buf, void* handle);
 TQ_API int tq_peer_ipc_open(const void* handle, void** buf);
 TQ_API int tq_peer_ipc_close(void* buf);
 
-/* Zero the buffer's flags and the counters (stream-ordered).  Every rank must reset
- * before any rank's next peer-sum call, e.g. after a timeout. */
+/* Zero the buffer and the counters (stream-ordered).  Every rank must reset before any
+ * rank's next peer-sum call, e.g. after a timeout. */
 TQ_API int tq_peer_reset(void* buf, int world, int slots, uint32_t* epochs, void* stream);
 
 /* tq_gemm_mixed on the decode kernel (1..16 rows, split_k 0..8) for this rank's K slice,

@@ -1,7 +1,7 @@
 """Row-parallel peer sum on one GPU.
 
-* world 1: the peer-sum form of the decode kernel (partial written to the exchange,
-  flag published, waited for, summed) gives the same bits as the decode kernel, over
+* world 1: the peer-sum form of the decode kernel (partial written to the exchange
+  with its call number, waited for, summed) gives the same bits as the decode kernel, over
   consecutive calls (both call-parity buffers) and CUDA-graph replays;
 * a wait that nothing will satisfy -- world 2 where the second "rank" is a buffer no
   kernel ever writes -- ends at the timeout with TQ_ERR_TIMEOUT in the error word and

@@ -72,9 +72,9 @@ def test_host_side_argument_checks(lib):
 
 
 def test_peer_sum_host_side_checks(lib):
-    # exchange layout: u32 flags [world][slots] padded to 256 B, then f32 [2][world][slots][256]
-    assert lib.tq_peer_buffer_bytes(2, 1024) == 8192 + 2 * 2 * 1024 * 256 * 4
-    assert lib.tq_peer_buffer_bytes(3, 5) == 256 + 2 * 3 * 5 * 256 * 4
+    # exchange layout: 16-byte words {v, call, v, call} [2][world][slots][128]
+    assert lib.tq_peer_buffer_bytes(2, 1024) == 2 * 2 * 1024 * 128 * 16
+    assert lib.tq_peer_buffer_bytes(3, 5) == 2 * 3 * 5 * 128 * 16
     assert lib.tq_peer_buffer_bytes(0, 16) == 0 and lib.tq_peer_buffer_bytes(9, 16) == 0
     assert lib.tq_peer_buffer_bytes(2, 0) == 0 and lib.tq_peer_buffer_bytes(2, 65537) == 0
     out = ctypes.c_void_p()

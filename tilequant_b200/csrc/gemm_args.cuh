@@ -43,13 +43,12 @@ struct RowsArgs {
   int64_t peer_timeout_ns;  // bound of every wait for a peer's partial
 };
 
-// Exchange buffer of the peer sum: flags u32 [world][slots] (padded to 256 bytes), then
-// partials f32 [2 (call parity)][world (source rank)][slots][256 (16 rows x 16 columns)].
-__host__ __device__ inline int64_t peer_flag_bytes(int world, int slots) {
-  return (((int64_t)world * slots * 4 + 255) / 256) * 256;
-}
+// Exchange buffer of the peer sum: 16-byte words [2 (call parity)][world (source rank)]
+// [slots][PEER_WORDS]; word i of a slot holds partial values 2i and 2i+1 (of the 16 rows
+// x 16 columns) interleaved with the call number: {v0, call, v1, call}.
+constexpr int PEER_WORDS = 128;
 __host__ __device__ inline int64_t peer_buffer_bytes(int world, int slots) {
-  return peer_flag_bytes(world, slots) + (int64_t)2 * world * slots * 256 * 4;
+  return (int64_t)2 * world * slots * PEER_WORDS * 16;
 }
 
 }  // namespace tq

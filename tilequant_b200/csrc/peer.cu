@@ -68,7 +68,7 @@ extern "C" int tq_peer_reset(void* buf, int world, int slots, uint32_t* epochs, 
   const int64_t bytes = tq_peer_buffer_bytes(world, slots);
   if (!buf || !epochs || bytes == 0) return tq_set_error(TQ_ERR_INVALID, "peer reset: bad buffer, counters or sizes");
   cudaStream_t st = (cudaStream_t)stream;
-  TQ_CUDA_TRY(cudaMemsetAsync(buf, 0, (size_t)tq::peer_flag_bytes(world, slots), st));
+  TQ_CUDA_TRY(cudaMemsetAsync(buf, 0, (size_t)bytes, st));
   TQ_CUDA_TRY(cudaMemsetAsync(epochs, 0, (size_t)slots * sizeof(uint32_t), st));
   return TQ_OK;
 }

@@ -27,7 +27,7 @@ import torch
 from . import _native as N
 from .gemm import _check_common
 
-DEFAULT_SLOTS = 2048  # decode CTAs of one call: 4 per 64-row output tile (M <= 32768)
+DEFAULT_SLOTS = 1024  # decode CTAs of one call: 4 per 64-row output tile (M <= 16384)
 
 
 class PeerExchange:
@@ -109,7 +109,7 @@ class PeerExchange:
         return int(self.err.item())
 
     def reset(self) -> None:
-        """Zero this rank's flags, counters and error word (stream-ordered).  Every rank
+        """Zero this rank's buffer, counters and error word (stream-ordered).  Every rank
         resets, then synchronizes with the others, before the next peer-sum call."""
         N.check(N.load().tq_peer_reset(ctypes.c_void_p(self._own), self.world, self.slots, self.epochs.data_ptr(),
                                        N.stream_of(self.epochs)), "PeerExchange.reset")
