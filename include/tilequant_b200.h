@@ -211,6 +211,34 @@ TQ_API int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const float
                                   int n_tc, int split_k, float* const* peer_bufs, uint32_t* epochs, int world,
                                   int rank, int slots, int64_t timeout_ns, int* err, void* stream);
 
+/* No counterpart in the reference.  tq_gemm_mixed_peer_sum for callers that cannot call
+ * cudaMalloc: serving runtimes that give all free device memory to their own pools at
+ * start-up, and real-time host loops that cannot take the device synchronization an
+ * allocation may cause.  Nothing is allocated: the exchange words, call counters and
+ * exchange-address table live in one file-scope __device__ array of
+ * TQ_NOALLOC_SCRATCH_BYTES (about 4 MB) that every GPU loading the library holds until
+ * the process exits.  A world of one GPU (the current device): that array cannot be
+ * reached from other GPUs, so sums across GPUs need tq_peer_alloc's buffers.  1..16
+ * rows and m <= 16384 (256 row tiles, 1024 CTA slots); larger requests are rejected
+ * (TQ_ERR_INVALID) before anything runs.  The first call on a device looks up the
+ * array's address and writes its table with a synchronous copy, so make it before any
+ * stream capture.  Every call shares the array, which keeps the last call's state (the
+ * call counters advance; each call's words carry its number, so nothing needs clearing
+ * between calls): calls whose kernels overlap on the GPU race.  reset_only != 0 zeroes
+ * the counters and words (e.g. after a timeout) and launches nothing.  Otherwise the
+ * contract and the result of tq_gemm_mixed_peer_sum with world 1 (the same bits as
+ * tq_gemm_mixed on the decode kernel). */
+#define TQ_NOALLOC_SLOTS 1024
+#define TQ_NOALLOC_SCRATCH_BYTES 4198656
+TQ_API int tq_gemm_mixed_peer_sum_noalloc(const int8_t* x_i8, int64_t ld_x8, const float* sx,
+                                          const int8_t* int8_tiles, const float* int8_scales,
+                                          const int32_t* int8_tile_ids, const int32_t* int8_row_ptr, int64_t t8,
+                                          const void* x_fp, int64_t ld_xfp, const void* fp16_tiles,
+                                          const int32_t* fp16_tile_ids, const int32_t* fp16_row_ptr, int64_t t16,
+                                          int fp_dtype, void* out, int64_t ldo, int out_dtype, const void* bias,
+                                          int64_t n_rows, int64_t m, int64_t k, int n_tr, int n_tc, int split_k,
+                                          int64_t timeout_ns, int reset_only, int* err, void* stream);
+
 /* ---------------------------------------------------------------- calibration */
 
 /* tile_scores[r, c] += sum over the tile of |f32(W) * f32(G)| (f32 [n_tr][n_tc]).

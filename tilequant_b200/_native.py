@@ -51,6 +51,8 @@ SIGNATURES = {
     "tq_peer_reset": [_P, _I, _I, _P, _P],
     "tq_gemm_mixed_peer_sum": [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I, _P, _I64, _I, _P,
                                _I64, _I64, _I64, _I, _I, _I, _P, _P, _I, _I, _I, _I64, _P, _P],
+    "tq_gemm_mixed_peer_sum_noalloc": [_P, _I64, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P, _P, _I64, _I, _P, _I64,
+                                       _I, _P, _I64, _I64, _I64, _I, _I, _I, _I64, _I, _P, _P],
 }
 
 TQ_PEER_MAX_WORLD, TQ_PEER_MAX_SLOTS, TQ_IPC_HANDLE_BYTES = 8, 65536, 64

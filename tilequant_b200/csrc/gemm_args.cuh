@@ -47,7 +47,7 @@ struct RowsArgs {
 // [slots][PEER_WORDS]; word i of a slot holds partial values 2i and 2i+1 (of the 16 rows
 // x 16 columns) interleaved with the call number: {v0, call, v1, call}.
 constexpr int PEER_WORDS = 128;
-__host__ __device__ inline int64_t peer_buffer_bytes(int world, int slots) {
+__host__ __device__ constexpr int64_t peer_buffer_bytes(int world, int slots) {
   return (int64_t)2 * world * slots * PEER_WORDS * 16;
 }
 
