@@ -1,0 +1,46 @@
+"""Decision-directory writing (no GPU): top-k archives per keep fraction in the
+reference's layout (src/quantization/decisions.py:174-224), readable by the loader."""
+
+from __future__ import annotations
+
+import json
+import math
+
+import numpy as np
+import pytest
+
+from tests.loader_fixtures import save_checkpoint, tiny_model
+from tilequant_b200.decisions import DEFAULT_KEEP_FRACS, infer_model_type, keep_tag, save_masks, score_npz_path
+from tilequant_b200.mask_io import load_fp16_keep_ids_for_layer
+
+
+def test_keep_tags_and_paths(tmp_path):
+    assert [keep_tag(f) for f in DEFAULT_KEEP_FRACS] == ["keep01", "keep02", "keep05", "keep10", "keep20"]
+    assert score_npz_path(tmp_path, "iaa").name == "iaa_tile_scores_tile64x64.npz"
+
+
+def test_save_masks_topk_per_fraction(tmp_path):
+    rng = np.random.default_rng(0)
+    scores = {"model_layers_0_self_attn_q_proj": rng.random((4, 4)).astype(np.float32),
+              "model_layers_0_mlp_down_proj": rng.random((4, 11)).astype(np.float32)}
+    dirs = save_masks(tmp_path, scores, DEFAULT_KEEP_FRACS, "tiny", "synthetic", "-", "gi")
+    for frac, d in dirs.items():
+        meta = json.loads((d / "meta.json").read_text())
+        assert meta["keep_frac"] == frac and meta["mask_rule"] == "topk_by_importance" and meta["quant_style"] == "gi"
+        for stem, s in scores.items():
+            ids, grid = load_fp16_keep_ids_for_layer(d, stem.replace("_", "."))  # stems map back to names
+            assert grid == s.shape
+            k = max(1, math.ceil(frac * s.size))
+            assert ids.numel() == k
+            kept = set(ids.tolist())
+            flat = s.reshape(-1)
+            assert min(flat[list(kept)]) >= max([flat[i] for i in range(s.size) if i not in kept], default=-1.0)
+
+
+def test_infer_model_type(tmp_path):
+    assert infer_model_type(save_checkpoint(tiny_model("llama"), tmp_path / "l", sharded=False)) == "llama"
+    assert infer_model_type(save_checkpoint(tiny_model("qwen2"), tmp_path / "q", sharded=False)) == "qwen"
+    (tmp_path / "x").mkdir()
+    (tmp_path / "x" / "config.json").write_text(json.dumps({"model_type": "gpt2"}))
+    with pytest.raises(RuntimeError):
+        infer_model_type(tmp_path / "x")
