@@ -195,11 +195,13 @@ TQ_API int tq_peer_ipc_close(void* buf);
  * rank's next peer-sum call, e.g. after a timeout. */
 TQ_API int tq_peer_reset(void* buf, int world, int slots, uint32_t* epochs, void* stream);
 
-/* tq_gemm_mixed on the decode kernel (1..16 rows, split_k 0..8) for this rank's K slice,
- * with the world ranks' FP32 partials summed in rank order 0..world-1 inside the kernel
- * before the output rounding and the bias: every rank gets the same (n_rows, m) output.
+/* tq_gemm_mixed on the decode kernel (1..64 rows as 16-row blocks, split_k 0..8) for this
+ * rank's K slice, with the world ranks' FP32 partials summed in rank order 0..world-1
+ * inside the kernel before the output rounding and the bias: every rank gets the same
+ * (n_rows, m) output.
  * Every rank must make the same sequence of calls (same n_rows, m, n_tr).  Needs
- * 4 * n_tr <= slots and all 4 * n_tr CTAs resident at once (else TQ_ERR_UNSUPPORTED).
+ * 4 * n_tr * ceil(n_rows / 16) <= slots and all those CTAs resident at once (else
+ * TQ_ERR_UNSUPPORTED).
  * A wait for a peer that exceeds timeout_ns writes TQ_ERR_TIMEOUT to `err` and the
  * output is then undefined; reset the exchange on every rank before going on. */
 TQ_API int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* int8_tiles,

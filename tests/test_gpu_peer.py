@@ -122,13 +122,36 @@ def test_missing_peer_times_out_with_status(cuda_device):
         silent.close()
 
 
+@pytest.mark.parametrize("rows", [17, 40, 64])
+def test_world1_peer_sum_row_blocks_match_row_kernel(cuda_device, rows):
+    """17..64 rows run as 16-row blocks; at the same split the sums are the split-K row
+    kernel's, bit for bit."""
+    m, k = 1536, 2048
+    p = _pack(m, k, 0.05, 15)
+    ex = PeerExchange(DEV, world=1, rank=0).connect_local()
+    bias = (torch.randn(m, generator=I.gen(4)) * 0.5).to(DEV, torch.bfloat16)
+    try:
+        for call in range(2):
+            x = I.activations(rows, k, 40 + call).to(DEV)
+            q, sx = tq.quantize_activation_tile_absmax(x)
+            want = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, out_dtype=torch.bfloat16, bias=bias,
+                                             split_k=4, algo=N.TQ_ALGO_ROWS, **_weights(p))
+            got = gemm_mixed_peer_sum(x_fp=x, x_int8=q, sx=sx, out_dtype=torch.bfloat16, bias=bias, split_k=4,
+                                      exchange=ex, **_weights(p))
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), want.view(torch.int16)), call
+        assert ex.status() == N.TQ_OK
+    finally:
+        ex.close()
+
+
 def test_peer_sum_host_side_rejections(cuda_device):
-    x = I.activations(17, 512, 32).to(DEV)
+    x = I.activations(65, 512, 32).to(DEV)
     q, sx = tq.quantize_activation_tile_absmax(x)
     p = _pack(256, 512, 0.0, 14)
     ex = PeerExchange(DEV, world=1, rank=0).connect_local()
     try:
-        with pytest.raises(N.TileQuantError):  # more than 16 rows: not a decode call
+        with pytest.raises(N.TileQuantError):  # more than 64 rows: not a decode call
             gemm_mixed_peer_sum(x_fp=x, x_int8=q, sx=sx, out_dtype=torch.bfloat16, exchange=ex, **_weights(p))
     finally:
         ex.close()

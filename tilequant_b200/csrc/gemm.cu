@@ -9,6 +9,7 @@ int tq_umma_supported(int64_t n_rows, int64_t m, int64_t k, const int8_t* x_i8, 
                       int64_t ld_xfp, const void* w8, const void* w16);
 int tq_launch_umma(const tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 int tq_gemv_supported(const tq::RowsArgs& a);
+int tq_gemv_peer_supported(const tq::RowsArgs& a);
 int tq_launch_gemv(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -120,7 +121,7 @@ extern "C" int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const f
   if (!peer_bufs || !epochs || slots < 1 || timeout_ns <= 0)
     return tq_set_error(TQ_ERR_INVALID, "peer sum: exchange buffers, counters, slots and timeout are required");
   if (n_rows == 0) return TQ_OK;  // every rank sees the same n_rows, so all skip together
-  if (!tq_gemv_supported(a)) return tq_set_error(TQ_ERR_UNSUPPORTED, "peer sum: needs 1..16 rows and split_k <= 8");
+  if (!tq_gemv_peer_supported(a)) return tq_set_error(TQ_ERR_UNSUPPORTED, "peer sum: needs 1..64 rows and split_k <= 8");
   a.peer_bufs = peer_bufs;
   a.peer_epochs = epochs;
   a.world = world;

@@ -114,7 +114,8 @@ __device__ __forceinline__ void load_w(const RowsArgs& a, WChunk<N>& c, int p0, 
 
 // Activations of a chunk and its MMAs.
 template <int N>
-__device__ __forceinline__ void run_chunk(const RowsArgs& a, const WChunk<N>& c, float (&acc)[2][4], int g, int t) {
+__device__ __forceinline__ void run_chunk(const RowsArgs& a, const WChunk<N>& c, float (&acc)[2][4], int g, int t,
+                                          int rb) {
   uint4 xa[N][2];
   float sc[N];
   int col[N];  // the loads of the whole chunk are issued before any of them is used
@@ -125,7 +126,7 @@ __device__ __forceinline__ void run_chunk(const RowsArgs& a, const WChunk<N>& c,
     if (u < c.n) {
 #pragma unroll
         for (int nb = 0; nb < 2; ++nb) {
-          const int row = nb * 8 + g;
+          const int row = rb + nb * 8 + g;
           xa[u][nb] = row < a.n_rows ? ldg16_row(reinterpret_cast<const uint8_t*>(a.x_i8) + (int64_t)row * a.ld_x8,
                                                  col[u] * 64 + 16 * t, a.K, a.a8_vec != 0)
                                      : make_uint4(0u, 0u, 0u, 0u);
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
   __shared__ float part[MAX_S * PSTRIDE];
   const int S = blockDim.x >> 5;
   const int r = blockIdx.x >> 2, m = blockIdx.x & 3;
+  const int rb = blockIdx.y * 16;  // first activation row of this CTA's 16-row block
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int wr = 16 * m + g;  // this thread's weight rows in the tile: wr and wr + 8
 
@@ -181,11 +183,11 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
   WChunk<UC> ch;
   load_w(a, ch, lo8, hi8, wr, t);
   grid_dep_wait();  // activations (and their scales) come from the preceding kernel
-  run_chunk(a, ch, acc, g, t);
+  run_chunk(a, ch, acc, g, t, rb);
 #pragma unroll 1
   for (int p0 = lo8 + UC; p0 < hi8; p0 += UC) {
     load_w(a, ch, p0, hi8, wr, t);
-    run_chunk(a, ch, acc, g, t);
+    run_chunk(a, ch, acc, g, t, rb);
   }
 
   // 16-bit tiles of this split, each as two 32-column halves (m16n8k16, FP32 accumulate)
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
       const uint4 whi = ldg16(tile + (wr + 8) * 64 + half * 32 + 8 * t);
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
-        const int row = nb * 8 + g;
+        const int row = rb + nb * 8 + g;
         uint4 xb = make_uint4(0u, 0u, 0u, 0u);
         if (row < a.n_rows)
           xb = ldg16_row(reinterpret_cast<const uint8_t*>(a.x_fp) + (int64_t)row * a.ld_xfp * 2,
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
       for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
       red[e] = v;
     }
-    const int b = blockIdx.x, W = a.world, slots = a.peer_slots;
+    const int b = blockIdx.y * gridDim.x + blockIdx.x, W = a.world, slots = a.peer_slots;
     if (tid == 0) {  // only this CTA of this rank touches its counter; launches are stream-ordered
       const uint32_t ep = a.peer_epochs[b] + 1u;
       a.peer_epochs[b] = ep;
@@ -268,11 +270,11 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
       for (int h = 0; h < 2; ++h) {
         const int e = 2 * w + h, j = e >> 4, tok = e & 15;
         const int cc = r * 64 + 16 * m + j;
-        if (tok < a.n_rows && cc < a.M && a.out) {
+        if (rb + tok < a.n_rows && cc < a.M && a.out) {
           const int ot = a.out_dtype;
           uint16_t y = f2h(v[h], ot);
           if (a.bias) y = f2h(h2f(y, ot) + h2f(reinterpret_cast<const uint16_t*>(a.bias)[cc], ot), ot);
-          reinterpret_cast<uint16_t*>(a.out)[(int64_t)tok * a.ldo + cc] = y;
+          reinterpret_cast<uint16_t*>(a.out)[(int64_t)(rb + tok) * a.ldo + cc] = y;
         }
       }
     }
@@ -283,11 +285,11 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
     float v = part[e];
     for (int s = 1; s < S; ++s) v += part[s * PSTRIDE + e];  // split order, reference :170-176
     const int cc = r * 64 + 16 * m + j;
-    if (tok < a.n_rows && cc < a.M && a.out) {
+    if (rb + tok < a.n_rows && cc < a.M && a.out) {
       const int ot = a.out_dtype;
       uint16_t y = f2h(v, ot);
       if (a.bias) y = f2h(h2f(y, ot) + h2f(reinterpret_cast<const uint16_t*>(a.bias)[cc], ot), ot);
-      reinterpret_cast<uint16_t*>(a.out)[(int64_t)tok * a.ldo + cc] = y;
+      reinterpret_cast<uint16_t*>(a.out)[(int64_t)(rb + tok) * a.ldo + cc] = y;
     }
   }
 }
@@ -308,12 +310,17 @@ int tq_gemv_supported(const RowsArgs& a) {
   return a.n_rows > 0 && a.n_rows <= 16 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
 }
 
+// The peer-sum form also takes up to 64 rows, as 16-row blocks along the grid's y.
+int tq_gemv_peer_supported(const RowsArgs& a) {
+  return a.n_rows > 0 && a.n_rows <= 64 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
+}
+
 template <int XT, bool PEER>
 static int launch_gemv_t(const RowsArgs& a, const cudaLaunchConfig_t& cfg) {
   if (PEER) {  // a waiting CTA must never hold the SM a later CTA of its grid needs
     int per_sm = 0;
     TQ_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<XT, PEER>, cfg.blockDim.x, 0));
-    if ((int64_t)per_sm * tq_sm_count() < (int64_t)cfg.gridDim.x)
+    if ((int64_t)per_sm * tq_sm_count() < (int64_t)cfg.gridDim.x * cfg.gridDim.y)
       return tq_set_error(TQ_ERR_UNSUPPORTED, "peer sum: the decode grid does not fit on the GPU at once");
   }
   TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<XT, PEER>, a));
@@ -328,7 +335,8 @@ int tq_launch_gemv(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st) {
   if (a.split < 1 || a.split > gv::MAX_S) return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: split_k must be in 1..8");
   if ((int64_t)n_tr * 4 > INT32_MAX) return tq_set_error(TQ_ERR_INVALID, "too many row tiles");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(n_tr * 4), 1, 1);
+  const int row_blocks = (a.n_rows + 15) / 16;  // 1 on the plain decode path (<= 16 rows)
+  cfg.gridDim = dim3((unsigned)(n_tr * 4), (unsigned)row_blocks, 1);
   cfg.blockDim = dim3(32 * a.split, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
@@ -341,7 +349,7 @@ int tq_launch_gemv(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  if (a.world > 0 && (int64_t)n_tr * 4 > a.peer_slots)
+  if (a.world > 0 && (int64_t)n_tr * 4 * row_blocks > a.peer_slots)
     return tq_set_error(TQ_ERR_INVALID, "peer sum: more decode CTAs than exchange slots");
   const bool peer = a.world > 0;
   int rc;

@@ -78,6 +78,7 @@ extern "C" int tq_gemm_mixed_peer_sum_noalloc(
     TQ_CUDA_TRY(cudaMemsetAsync(base + kCountOff, 0, kBytes - kCountOff, (cudaStream_t)stream));
     return TQ_OK;
   }
+  if (n_rows > 16) return tq_set_error(TQ_ERR_UNSUPPORTED, "no-alloc peer sum: needs 1..16 rows");
   if ((int64_t)n_tr * 4 > TQ_NOALLOC_SLOTS)
     return tq_set_error(TQ_ERR_INVALID, "no-alloc peer sum: more than 256 row tiles (m > 16384) exceeds the "
                                         "scratch array's 1024 CTA slots");

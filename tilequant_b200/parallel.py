@@ -12,7 +12,7 @@ columns):
   unchanged per-tile scales, quantizes only those activation columns (the same codes
   and scales the full GEMM computes for them), and the partial outputs are summed
   with one NCCL all-reduce per layer; a bias is added once, after the sum.  With a
-  ``PeerExchange`` (``peer.py``), decode-sized calls (1..16 rows) sum the partials
+  ``PeerExchange`` (``peer.py``), decode-sized calls (1..64 rows) sum the partials
   inside the decode GEMM instead, over NVLink, in FP32 and in rank order.
 
 Attention heads: rank r of t owns query heads [q0, q1) and the KV heads they read.
@@ -100,12 +100,12 @@ def _slice_linear(lin: nn.Linear, rows: Optional[Tuple[int, int]] = None,
 
 
 class PeerReduceSum(nn.Module):
-    """Row-parallel ``MixedLinear`` whose decode-sized calls (1..16 rows) sum the ranks'
+    """Row-parallel ``MixedLinear`` whose decode-sized calls (1..64 rows) sum the ranks'
     partials inside the GEMM through a ``PeerExchange``; larger calls take the NCCL
     all-reduce of ``AllReduceSum``.  The bias is added once, after the sum, either way.
     Every rank sees the same row counts, so all ranks take the same path."""
 
-    MAX_ROWS = 16
+    MAX_ROWS = 64
 
     def __init__(self, inner: nn.Module, exchange, group=None, bias: Optional[torch.Tensor] = None):
         super().__init__()

@@ -4,7 +4,7 @@ partial outputs itself, over NVLink, in place of a separate all-reduce.
 No counterpart in the reference, which runs on one GPU.  A tensor-parallel O or down
 projection (``parallel.py``) gives each rank a slice of the input columns, so each
 rank's GEMM yields a partial output that has to be summed over the ranks.  With a
-``PeerExchange`` the decode kernel (1..16 activation rows) writes its FP32 partial
+``PeerExchange`` the decode kernel (1..64 activation rows) writes its FP32 partial
 tiles straight into every rank's exchange buffer, waits for the other ranks' tiles of
 the same output block (bounded by ``timeout_s``; a timeout sets an error word, it
 never hangs), and sums them in rank order before rounding: every rank ends up with
@@ -154,7 +154,7 @@ def gemm_mixed_peer_sum(
 ) -> torch.Tensor:
     """``gemm_mixed_rows_splitk`` on this rank's K slice, summed over the exchange's
     ranks inside the kernel (rank order, FP32), then rounded and ``bias`` added: the
-    same (N, M) result on every rank.  1..16 rows; every rank makes the same calls."""
+    same (N, M) result on every rank.  1..64 rows; every rank makes the same calls."""
     device = N.require_cuda(x_fp, x_int8, sx, int8_tiles, fp16_tiles, out, bias)
     if exchange.bufs is None:
         raise ValueError("the exchange is not connected")
