@@ -639,7 +639,8 @@ def run_generate(args, ws, rank, device):
         "config": {"workload": f"config {'3' if args.model == 'llama3b' else ('4' if args.model == 'qwen7b' else '5')}:"
                                f" {args.model}", "layers": layers, "keep_bf16": spec["keep"], "batch": B,
                    "prompt": P, "new_tokens": T,
-                   "parallelism": (f"tp{ws} (" + ("O/down sums inside the decode GEMM over NVLink for <= 16 rows, "
+                   "parallelism": (f"tp{ws} (" + ("O/down sums inside the decode GEMM over NVLink where the "
+                                                  "decode grid fits (<= 64 rows), "
                                                   "NCCL all-reduce otherwise)" if exchange is not None else
                                                   "NCCL all-reduce after O and down)")) if tp else f"replicas x{ws}",
                    "l2": "weights (GBs) and KV cache exceed L2 every step"},

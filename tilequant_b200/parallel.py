@@ -101,9 +101,12 @@ def _slice_linear(lin: nn.Linear, rows: Optional[Tuple[int, int]] = None,
 
 class PeerReduceSum(nn.Module):
     """Row-parallel ``MixedLinear`` whose decode-sized calls (1..64 rows) sum the ranks'
-    partials inside the GEMM through a ``PeerExchange``; larger calls take the NCCL
-    all-reduce of ``AllReduceSum``.  The bias is added once, after the sum, either way.
-    Every rank sees the same row counts, so all ranks take the same path."""
+    partials inside the GEMM through a ``PeerExchange``; larger calls, and shapes whose
+    decode grid does not fit the exchange's slots or the GPU at once (the kernel refuses
+    those on the host, before any launch, the same way on every rank; the answer is kept
+    per shape), take the NCCL all-reduce of ``AllReduceSum``.  The bias is added once,
+    after the sum, either way.  Every rank sees the same row counts, so all ranks take
+    the same path."""
 
     MAX_ROWS = 64
 
@@ -113,25 +116,33 @@ class PeerReduceSum(nn.Module):
         self.exchange = exchange
         self.group = group
         self.bias = None if bias is None else nn.Parameter(bias.detach().clone(), requires_grad=False)
+        self._peer_fits: Dict[int, bool] = {}  # rows -> the peer-sum grid fits
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
 
+        from ._native import TileQuantError
         from .peer import gemm_mixed_peer_sum
         from .quant_utils import quantize_activation_tile_absmax
 
         inner = self.inner
         rows = x.numel() // max(1, x.shape[-1])
-        if 0 < rows <= self.MAX_ROWS and x.dim() in (2, 3):
+        if 0 < rows <= self.MAX_ROWS and x.dim() in (2, 3) and self._peer_fits.get(rows, True):
             x2d = x.reshape(-1, x.shape[-1]).contiguous()
             if x2d.shape[1] != inner.K_orig:
                 raise ValueError(f"Input K mismatch: got {x2d.shape[1]}, expected {inner.K_orig}")
             out_dtype = inner._out_dtype()
             bias = None if self.bias is None else self.bias.to(dtype=out_dtype).contiguous()
             x_int8, sx = quantize_activation_tile_absmax(x2d, tile_n=inner.tile_n)
-            y = gemm_mixed_peer_sum(x_fp=x2d, x_int8=x_int8, sx=sx, out_dtype=out_dtype, exchange=self.exchange,
-                                    bias=bias, **inner._weights())
-            return y.reshape(*x.shape[:-1], inner.M_orig)
+            try:
+                y = gemm_mixed_peer_sum(x_fp=x2d, x_int8=x_int8, sx=sx, out_dtype=out_dtype, exchange=self.exchange,
+                                        bias=bias, **inner._weights())
+                self._peer_fits[rows] = True
+                return y.reshape(*x.shape[:-1], inner.M_orig)
+            except (ValueError, TileQuantError) as e:
+                if "peer sum:" not in str(e) or rows in self._peer_fits:
+                    raise
+                self._peer_fits[rows] = False  # this shape's grid does not fit: NCCL from now on
         y = inner(x)
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(y, group=self.group)
