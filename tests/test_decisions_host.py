@@ -44,3 +44,27 @@ def test_infer_model_type(tmp_path):
     (tmp_path / "x" / "config.json").write_text(json.dumps({"model_type": "gpt2"}))
     with pytest.raises(RuntimeError):
         infer_model_type(tmp_path / "x")
+
+
+def test_resolve_decision_and_keep_dirs(tmp_path):
+    import os
+    import time
+
+    from tilequant_b200.decisions import resolve_decision_and_keep_dir, resolve_decision_dir, resolve_keep_dir
+
+    with pytest.raises(RuntimeError, match="Decision directory not found"):
+        resolve_decision_dir(tmp_path / "Model-X", "gi", tmp_path / "Decision")
+    d = tmp_path / "Decision" / "Model-X" / "gi"
+    (d / "tile_masks" / "keep01").mkdir(parents=True)
+    (d / "tile_masks" / "keep05").mkdir()
+    (d / "tile_masks" / "other").mkdir()
+    t = time.time()
+    os.utime(d / "tile_masks" / "keep01", (t - 100, t - 100))
+    os.utime(d / "tile_masks" / "keep05", (t, t))
+    assert resolve_decision_dir(tmp_path / "Model-X", "GI", tmp_path / "Decision") == d.resolve()
+    assert resolve_keep_dir(d).name == "keep05"  # the newest keepNN
+    assert resolve_keep_dir(d, "keep01").name == "keep01"
+    with pytest.raises(RuntimeError, match="Requested keep dir not found"):
+        resolve_keep_dir(d, "keep99")
+    dd, kd = resolve_decision_and_keep_dir(tmp_path / "Model-X", "gi", "keep01", tmp_path / "Decision")
+    assert (dd, kd.name) == (d.resolve(), "keep01")

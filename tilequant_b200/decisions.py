@@ -23,6 +23,7 @@ from types import SimpleNamespace
 from typing import Dict, Iterable, Optional, Sequence
 
 import numpy as np
+import torch
 import torch.nn as nn
 
 from .calibrate import collect_gi_tile_scores, collect_iaa_tile_scores_with_channel_stats, topk_mask
@@ -161,3 +162,74 @@ def build_decisions_from_batches(model: nn.Module, batches: Iterable, decision_d
     _replace_atomically(decision_dir / "decision_ready.flag", lambda tmp: tmp.write_text("done\n", encoding="utf-8"))
     _prune_progress_files(decision_dir)
     return decision_dir
+
+
+# ------------------------------------------------------------------ resolution
+
+def resolve_decision_dir(local_model_dir, quant_style: str, decision_root="Decision") -> Path:
+    """``<decision_root>/<model dir name>/<style>``, which must exist (resolve.py:22-26)."""
+    d = Path(decision_root).resolve() / Path(local_model_dir).name / str(quant_style).lower()
+    if not d.exists():
+        raise RuntimeError(f"Decision directory not found: {d}")
+    return d
+
+
+def resolve_keep_dir(decision_dir, keep_tag: Optional[str] = None) -> Path:
+    """``tile_masks/<keep_tag>``, or the newest keepNN directory when no tag is given
+    (resolve.py:29-41)."""
+    root = Path(decision_dir) / "tile_masks"
+    if not root.exists():
+        raise RuntimeError(f"Mask root not found: {root}")
+    keep_dirs = [p for p in root.iterdir() if p.is_dir() and p.name.startswith("keep")]
+    if not keep_dirs:
+        raise RuntimeError(f"No keepXX folders found under: {root}")
+    if keep_tag is not None:
+        picked = root / keep_tag
+        if not picked.exists():
+            raise RuntimeError(f"Requested keep dir not found: {picked}")
+        return picked
+    return sorted(keep_dirs, key=lambda p: (p.stat().st_mtime, p.name), reverse=True)[0]
+
+
+def resolve_decision_and_keep_dir(local_model_dir, quant_style: str, keep_tag: Optional[str] = None,
+                                  decision_root="Decision"):
+    """resolve.py:44-51."""
+    d = resolve_decision_dir(local_model_dir, quant_style, decision_root)
+    return d, resolve_keep_dir(d, keep_tag)
+
+
+def load_model_and_tokenizer(model_dir, *, quant_style: str = "gi", keep_tag: Optional[str] = "keep01",
+                             dtype: str = "bf16", device="cuda", iaa_channel_stats_path: Optional[str] = None,
+                             decision_root="Decision", tile_m: int = 64, tile_n: int = 64,
+                             attn_implementation: Optional[str] = "sdpa"):
+    """The model of a local checkpoint with the tile maps of its existing decision
+    directory applied at load, its tokenizer, and a description (the reference's
+    application.load_model_and_tokenizer, application.py:58-139, for decision artifacts
+    that are already built; building them needs ``build_decisions_from_batches``)."""
+    from transformers import AutoTokenizer
+
+    from .loader import ApplyConfig, TileConfig, load_mixed_precision_model_from_masks
+
+    model_dir = Path(model_dir)
+    decision_dir, keep_dir = resolve_decision_and_keep_dir(model_dir, quant_style, keep_tag, decision_root)
+    model_type = infer_model_type(model_dir)
+    quant_style = str(quant_style).lower()
+    if quant_style == "iaa" and not iaa_channel_stats_path:
+        auto = decision_dir / "iaa_channel_mean_abs.npz"
+        if not auto.exists():
+            raise FileNotFoundError(f"IAA channel stats not found: {auto}")
+        iaa_channel_stats_path = str(auto)
+    tokenizer = AutoTokenizer.from_pretrained(str(model_dir), use_fast=True)
+    if tokenizer.pad_token is None:
+        tokenizer.pad_token = tokenizer.eos_token
+    device = torch.device(device)
+    model, stats = load_mixed_precision_model_from_masks(
+        model_dir, keep_dir,
+        ApplyConfig(model_type=model_type, dtype_out=dtype, tile=TileConfig(tile_m, tile_n), module_filters=[],
+                    quant_style=quant_style, iaa_channel_stats_path=iaa_channel_stats_path),
+        torch.float16 if dtype == "fp16" else torch.bfloat16, device, attn_implementation=attn_implementation)
+    info = {"device": device, "local_model_dir": model_dir, "decision_dir": decision_dir, "keep_dir": keep_dir,
+            "model_type": model_type, "quant_style": quant_style, "tile_m": tile_m, "tile_n": tile_n,
+            "iaa_channel_stats_path": iaa_channel_stats_path, "attn_implementation": attn_implementation,
+            "stats": stats}
+    return model, tokenizer, info
