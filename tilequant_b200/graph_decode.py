@@ -31,6 +31,8 @@ from typing import Optional, Sequence, Union
 import torch
 import torch.nn.functional as F
 
+from .trace import traced
+
 _ATTENTION_NAME = "tilequant_b200_static_graph"
 _DECODER_ATTRIBUTE = "_tilequant_b200_graph_decoder"
 # Prompts of more tokens than this (batch x prompt) prefill eagerly into the cache: the
@@ -267,6 +269,7 @@ class CudaGraphGreedyDecoder:
             raise ValueError(f"expected {(self.batch_size, self.prompt_tokens)}, got {tuple(prompt.shape)}")
         return prompt
 
+    @traced("tq.prefill")
     @torch.inference_mode()
     def prefill(self, prompt_ids: Union[torch.Tensor, Sequence[int]]) -> torch.Tensor:
         """Copy the prompt in, replay the reset-and-prefill graph; returns the first
@@ -282,6 +285,7 @@ class CudaGraphGreedyDecoder:
         self.last_logits = self._prefill_logits
         return self._prefill_logits if self._prefill_only else self._token
 
+    @traced("tq.decode")
     @torch.inference_mode()
     def decode(self, steps: Optional[int] = None) -> torch.Tensor:
         """Replay the decode graph ``steps`` times (default: up to the prepared bound);

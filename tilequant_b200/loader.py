@@ -31,6 +31,7 @@ from .mask_io import load_fp16_keep_ids_for_layer
 from .mixed_linear import MixedLinear, fuse_projection_groups
 from .pack import pack_weight_from_tile_ids
 from .rules import iter_target_linears
+from .trace import traced
 
 
 @dataclass(frozen=True)
@@ -180,6 +181,7 @@ def _cast(tensor: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return tensor.to(dtype=dtype) if tensor.is_floating_point() else tensor
 
 
+@traced("tq.load_mixed_precision_model_from_masks")
 def load_mixed_precision_model_from_masks(local_model_dir, keep_dir, apply_cfg: ApplyConfig,
                                           torch_dtype: torch.dtype, device,
                                           attn_implementation: Optional[str] = None):

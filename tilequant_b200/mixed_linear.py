@@ -38,6 +38,7 @@ from .quant_utils import (
     quantize_activation_tile_absmax,
     quantize_activation_tile_with_scales,
 )
+from .trace import traced
 
 # Rows per quantize+GEMM chunk of a large call (the reference's knob; the results do
 # not depend on it).  B200's 180 GB lets prefill run in far fewer, larger launches.
@@ -170,6 +171,7 @@ class MixedLinear(nn.Module):
         x_int8 = quantize_activation_tile_with_scales(x_chunk, sx=sx, tile_n=self.tile_n)
         self._gemm_bias(x_fp=x_chunk, x_int8=x_int8, sx=sx, out=out)
 
+    @traced("tq.MixedLinear")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         in_shape = x.shape
         if x.dim() == 3:
@@ -257,6 +259,7 @@ class MixedLinearSlice(nn.Module):
         self.out_features = self.stop - self.start
         self.in_features = group.linear.K_orig
 
+    @traced("tq.MixedLinearSlice")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return self.group.output_for(x, self.index)[..., self.start:self.stop]
 

@@ -34,6 +34,8 @@ from typing import Callable, Dict, List, Optional, Tuple
 import torch
 import torch.nn as nn
 
+from .trace import traced
+
 TILE = 64
 
 
@@ -118,6 +120,7 @@ class PeerReduceSum(nn.Module):
         self.bias = None if bias is None else nn.Parameter(bias.detach().clone(), requires_grad=False)
         self._peer_fits: Dict[int, bool] = {}  # rows -> the peer-sum grid fits
 
+    @traced("tq.PeerReduceSum")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
 
@@ -161,6 +164,7 @@ class AllReduceSum(nn.Module):
         self.group = group
         self.bias = None if bias is None else nn.Parameter(bias.detach().clone(), requires_grad=False)
 
+    @traced("tq.AllReduceSum")
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import torch.distributed as dist
 
