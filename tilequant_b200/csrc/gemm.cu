@@ -10,6 +10,7 @@ int tq_umma_supported(int64_t n_rows, int64_t m, int64_t k, const int8_t* x_i8, 
 int tq_launch_umma(const tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 int tq_gemv_supported(const tq::RowsArgs& a);
 int tq_gemv_peer_supported(const tq::RowsArgs& a);
+int tq_gemv_preferred(const tq::RowsArgs& a, int n_tr);
 int tq_launch_gemv(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -95,8 +96,10 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
       return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: unsupported shape or alignment");
     return tq_launch_umma(a, n_tr, fp_dtype, st);
   }
-  if (algo == TQ_ALGO_GEMV || (algo == TQ_ALGO_AUTO && tq_gemv_supported(a))) {
-    if (!tq_gemv_supported(a)) return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: needs <= 16 rows, aligned rows");
+  if (algo == TQ_ALGO_GEMV || (algo == TQ_ALGO_AUTO && tq_gemv_preferred(a, n_tr))) {
+    // asked for by name, the decode kernel also runs 17..64 rows as 16-row blocks
+    if (!(algo == TQ_ALGO_GEMV ? tq_gemv_peer_supported(a) : tq_gemv_supported(a)))
+      return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: needs <= 64 rows and split_k <= 8");
     return tq_launch_gemv(a, n_tr, fp_dtype, st);
   }
   if (algo != TQ_ALGO_AUTO && algo != TQ_ALGO_ROWS) return tq_set_error(TQ_ERR_INVALID, "unknown algo");

@@ -310,6 +310,26 @@ int tq_gemv_supported(const RowsArgs& a) {
   return a.n_rows > 0 && a.n_rows <= 16 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
 }
 
+// Whether the automatic choice for <= 16 rows is this kernel rather than the split-K
+// row kernel: measured on B200, it wins while its grid (4 CTAs per row tile) fits in one
+// wave and each warp holds at most 2 * U INT8 tiles (e.g. 3584 x 3584: 8.3 against
+// 10.7 us at 4 rows), and loses beyond (37888 x 3584: 69 against 40 us; 3584 x 18944:
+// 34 against 28 us), where the row kernel's bulk-copy stream keeps more bytes in flight.
+int tq_gemv_preferred(const RowsArgs& a, int n_tr) {
+  if (!tq_gemv_supported(a)) return 0;
+  const int split = a.split ? a.split : tq_gemv_split(a.n_tc);
+  if ((a.n_tc + split - 1) / split > 2 * gv::U) return 0;
+  static int per_sm[gv::MAX_S + 1] = {};  // resident CTAs per SM by split (the same on every B200)
+  if (!per_sm[split]) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<TQ_DTYPE_BF16, false>, 32 * split, 0) !=
+            cudaSuccess || n <= 0)
+      return 0;
+    per_sm[split] = n;
+  }
+  return (int64_t)n_tr * 4 <= (int64_t)per_sm[split] * tq_sm_count();
+}
+
 // The peer-sum form also takes up to 64 rows, as 16-row blocks along the grid's y.
 int tq_gemv_peer_supported(const RowsArgs& a) {
   return a.n_rows > 0 && a.n_rows <= 64 && !a.partials && !a.fused && a.split >= 0 && a.split <= gv::MAX_S;
