@@ -53,6 +53,8 @@ class PeerExchange:
             N.check(lib.tq_peer_alloc(self.world, self.slots, ctypes.byref(buf)), "PeerExchange")
         self._own: Optional[int] = buf.value
         self._opened: List[int] = []
+        self._connected = False  # mapped across processes by connect()
+        self._group = None
         self.epochs = torch.zeros(self.slots, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.bufs: Optional[torch.Tensor] = None  # int64 [world] device pointers, own at index rank
@@ -71,8 +73,8 @@ class PeerExchange:
         self.bufs = torch.tensor([int(p) for p in ptrs], dtype=torch.int64, device=self.device)
 
     def connect(self, group=None) -> "PeerExchange":
-        """Exchange IPC handles with the other ranks of ``group`` (collective) and map
-        their buffers."""
+        """Exchange IPC handles with the other ranks of ``group`` (collective; with the
+        NCCL backend, call it with this rank's device current) and map their buffers."""
         import torch.distributed as dist
 
         if dist.get_world_size(group) != self.world or dist.get_rank(group) != self.rank:
@@ -92,6 +94,8 @@ class PeerExchange:
                 self._opened.append(out.value)
                 ptrs.append(out.value)
         self._set_bufs(ptrs)
+        self._group = group
+        self._connected = True
         dist.barrier(group=group)
         return self
 
@@ -116,14 +120,20 @@ class PeerExchange:
         self.err.zero_()
 
     def close(self) -> None:
-        """Unmap the peers' buffers and free this one.  Call on every rank after a
-        barrier, once no rank has peer-sum work in flight."""
+        """Unmap the peers' buffers and free this one.  Call on every rank, once no rank
+        has peer-sum work in flight; after ``connect`` it is collective: every rank
+        unmaps, then all wait for each other before any buffer is freed."""
         lib = N.load()
         with torch.cuda.device(self.device):
             torch.cuda.synchronize(self.device)
             for p in self._opened:
                 lib.tq_peer_ipc_close(ctypes.c_void_p(p))
             self._opened = []
+            if self._connected:
+                import torch.distributed as dist
+
+                dist.barrier(group=self._group)  # no rank still maps this buffer
+                self._connected = False
             if self._own is not None:
                 lib.tq_peer_free(ctypes.c_void_p(self._own))
                 self._own = None
