@@ -19,7 +19,7 @@ import tilequant_b200 as tq
 from tilequant_b200 import _native as N
 from oracle import oracle as O
 from tests.golden import inputs as I
-from tests.helpers import assert_close_with_bias, assert_within_ulp, from_torch16, to_torch16, ulp_dist16
+from tests.helpers import assert_close_with_bias, assert_within_ulp, from_torch16, to_torch16
 
 pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"

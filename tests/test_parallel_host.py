@@ -3,7 +3,6 @@ a 2-rank (gloo) forward of a sharded dense decoder against the unsharded one."""
 
 from __future__ import annotations
 
-import os
 import socket
 
 import pytest
