@@ -46,7 +46,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 from tests.golden import inputs as I  # noqa: E402
 
-REF = Path(os.environ.get("TILEQUANT_REFERENCE", "/root/reference"))
+if not os.environ.get("TILEQUANT_REFERENCE"):
+    raise SystemExit("set TILEQUANT_REFERENCE to the reference checkout (see the module docstring)")
+REF = Path(os.environ["TILEQUANT_REFERENCE"])
 sys.path.insert(0, str(REF))
 
 import triton.language as tl  # noqa: E402
