@@ -392,6 +392,32 @@ def run_prefill(args, ws, rank, device):
     return line
 
 
+def decode_cpu_baseline(x, w, fp16, int8, n_tr, n_tc, bytes_per_call, seconds=3.0):
+    """Config 1 on the host cores: the C restatement of the reference (oracle/, OpenMP,
+    all host threads) quantizing the 16 tokens and running the full 3072 x 3072 mixed
+    GEMM, repeated for about ``seconds``; GB/s over the same bytes per call as the GPU
+    line."""
+    import numpy as np  # noqa: F401  (the oracle's arrays)
+    from oracle import oracle as O
+    from tests.golden import inputs as I
+
+    xb = I.bits(x)
+    pk = O.pack(I.bits(w), n_tr, n_tc, int8.numpy(), fp16.numpy())
+    m, k = w.shape
+    q, sx = O.quantize_act(xb)  # warm-up (loads the library, touches the arrays)
+    O.gemm(q, sx, pk, xb, m, k, split_k=1)
+    calls, spent = 0, 0.0
+    while spent < seconds or calls < 3:
+        t0 = time.perf_counter()
+        q, sx = O.quantize_act(xb)
+        O.gemm(q, sx, pk, xb, m, k, split_k=1)
+        spent += time.perf_counter() - t0
+        calls += 1
+    return {"value": round(bytes_per_call * calls / spent / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
+            "kind": "port", "sample": f"{calls} whole config-1 calls (quantize 16 x {k} + mixed GEMM {m} x {k}) through "
+                                      "oracle/tq_oracle.c (OpenMP)"}
+
+
 def run_decode(args, ws, rank, device):
     """Config 1: one q_proj-shaped MixedLinear (3072 x 3072, 1 % BF16), 16 tokens."""
     import tilequant_b200 as tq
@@ -435,6 +461,25 @@ def run_decode(args, ws, rank, device):
     us = _max_over_ranks(e0.elapsed_time(e1) * 1e3 / (args.steps * nrot), ws)
     gbs = ws * bytes_per / (us * 1e-6) / 1e9
     hbm = _peaks().get("hbm_gbs", 6543.1)
+
+    # ---- e2e: the same call through the module with the 16 tokens copied in from pinned
+    # host memory and the output copied back, every call (weights rotate as above)
+    host_x = x.pin_memory()
+    host_y = torch.empty((16, 3072), dtype=torch.bfloat16).pin_memory()
+    with torch.inference_mode():
+        for lin in lins[:3]:
+            host_y.copy_(lin(host_x.to(device, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        s0, s1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        s0.record()
+        for _ in range(max(1, args.steps // 10)):
+            for lin in lins:
+                host_y.copy_(lin(host_x.to(device, non_blocking=True)), non_blocking=True)
+        s1.record()
+        torch.cuda.synchronize()
+    e2e_us = _max_over_ranks(s0.elapsed_time(s1) * 1e3 / (max(1, args.steps // 10) * nrot), ws)
+    cpu = decode_cpu_baseline(x, w, fp16, int8, n_tr, n_tc, bytes_per) if (ws == 1 and rank == 0) else None
     return {
         "metric": "mixed tile GEMM GB/s: config 1 (q_proj 3072x3072, 16 tokens, 1 % BF16), quantize+GEMM",
         "value": round(gbs, 1), "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
@@ -449,6 +494,10 @@ def run_decode(args, ws, rank, device):
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs"},
         "gpu_launches": per_replay * args.steps,
         "clocks": clocks.summary(),
+        "e2e": {"value": round(ws * bytes_per / (e2e_us * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": nrot * 16 * 3072 * 2, "d2h_bytes_per_step": nrot * 16 * 3072 * 2,
+                "what": "MixedLinear calls with pinned host tokens in and outputs out, eagerly launched"},
+        **({"cpu_baseline": cpu} if cpu is not None else {}),
     }
 
 
