@@ -6,7 +6,10 @@
  * src/kernels/pack.py).  Every entry point takes plain device pointers, element
  * strides and a cudaStream_t passed as void*; nothing here allocates device memory
  * except tq_peer_alloc (the exchange buffer of the tensor-parallel peer sum).
- * All kernels are asynchronous on `stream` and may be captured in a CUDA graph.
+ * Kernel launches are asynchronous on `stream`.  The quantizer, GEMM (tq_gemm_mixed,
+ * tq_gemm_mixed_fused_quant, tq_gemm_mixed_peer_sum), packer and calibration entry
+ * points may be captured in a CUDA graph; the tq_peer_* set-up calls are synchronous
+ * host calls, and this statement does not cover tq_gemm_mixed_peer_sum_noalloc.
  *
  * Return value: TQ_OK (0) or a TQ_ERR_* code; tq_last_error() gives a message for
  * the calling thread's last failure.  Shape/argument problems are detected on the
