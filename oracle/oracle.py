@@ -61,7 +61,7 @@ def lib():
         L.tqo_quantize_with_scales.argtypes = [P, I, I64, I64, I64, I64, P, P]
         L.tqo_pack_int8.argtypes = [P, I, I64, I64, I64, I, P, I64, P, P, P]
         L.tqo_gemm_mixed.argtypes = [P, I64, P, P, P, P, P, P, I64, I, P, P, P, P, I64, I, P,
-                                     I64, I64, I64, I, I, I, I, P]
+                                     I64, I64, I64, I, I, I, I, P, P]
         L.tqo_calib_gi_accumulate.argtypes = [P, P, I, I64, I64, I, I, P]
         L.tqo_iaa_channel_accumulate.argtypes = [P, I, I64, I64, P]
         L.tqo_iaa_tile_scores.argtypes = [P, I, I64, I64, I, I, P, I64, P, P]
@@ -187,17 +187,19 @@ def select_split_k_reference(n_tr: int, n_blocks: int, n_tc: int, sm_count: int)
 
 
 def gemm(x_i8, sx, pk: dict, x_bits, M: int, K: int, *, split_k: int = 1, bias_bits=None,
-         xdtype: int = BF16, odtype: int = BF16, use_fma: bool = True, want_partials: bool = False):
+         xdtype: int = BF16, odtype: int = BF16, use_fma: bool = True, want_partials: bool = False,
+         want_f32: bool = False):
     """Restatement of the mixed GEMM (gemm_rows_splitk_64x64.py:108-190).
 
-    Returns the output as uint16 bits of ``odtype`` and optionally the INT32 tile
-    partials [t8, n_rows, 64]."""
+    Returns the output as uint16 bits of ``odtype``, then (when asked) the INT32 tile
+    partials [t8, n_rows, 64] and the FP32 sums before the output rounding [n_rows, M]."""
     x_i8 = np.ascontiguousarray(x_i8, np.int8)
     x_bits = np.ascontiguousarray(_h16(x_bits))
     n = x_i8.shape[0]
     out = np.zeros((n, M), np.uint16)
     t8 = pk["int8_tiles"].shape[0]
     parts = np.zeros((t8, n, 64), np.int32) if want_partials else None
+    acc = np.zeros((n, M), np.float32) if want_f32 else None
     w16 = np.ascontiguousarray(pk["fp16_tiles"], np.uint16)
     bias = None if bias_bits is None else np.ascontiguousarray(bias_bits, np.uint16)
     lib().tqo_gemm_mixed(
@@ -210,8 +212,31 @@ def gemm(x_i8, sx, pk: dict, x_bits, M: int, K: int, *, split_k: int = 1, bias_b
         _ptr(np.ascontiguousarray(pk["fp16_tile_ids"], np.int32)),
         _ptr(np.ascontiguousarray(pk["fp16_row_ptr"], np.int32)),
         _ptr(out), M, odtype, _ptr(bias), n, M, K, pk["n_tr"], pk["n_tc"], int(split_k),
-        1 if use_fma else 0, _ptr(parts))
-    return (out, parts) if want_partials else out
+        1 if use_fma else 0, _ptr(parts), _ptr(acc))
+    extra = ([parts] if want_partials else []) + ([acc] if want_f32 else [])
+    return tuple([out] + extra) if extra else out
+
+
+def peer_sum(partials_f32, odtype: int = BF16, bias_bits=None) -> np.ndarray:
+    """Row-parallel sum of the ranks' FP32 partial outputs, as the decode kernel's peer
+    sum forms it: added in rank order 0..world-1 in FP32, rounded to ``odtype``, then
+    the bias added the way the GEMM adds it.  (No counterpart in the reference, which
+    runs on one GPU.)"""
+    total = np.array(partials_f32[0], dtype=np.float32, copy=True)
+    for p in partials_f32[1:]:
+        total = (total + np.asarray(p, np.float32)).astype(np.float32)
+    out = _round16(total, odtype)
+    if bias_bits is not None:
+        b = h_to_f32(np.asarray(bias_bits, np.uint16), odtype)[None, :]
+        out = _round16((h_to_f32(out, odtype) + b).astype(np.float32), odtype)
+    return out
+
+
+def _round16(x: np.ndarray, dtype: int) -> np.ndarray:
+    """f32 -> 16-bit bits, round to nearest even."""
+    if dtype == BF16:
+        return f32_to_bf16_bits(x)
+    return np.ascontiguousarray(x, np.float32).astype(np.float16).view(np.uint16)
 
 
 # ------------------------------------------------------------------- calibration

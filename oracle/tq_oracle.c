@@ -179,14 +179,16 @@ void tqo_pack_int8(const uint16_t* w, int dtype, int64_t m, int64_t k, int64_t l
  *
  * x_i8 is (n_rows, K) with row stride ld_x8; x_fp (16-bit, xdtype) with row stride
  * ld_xfp; out (16-bit, odtype) with row stride ldo.  partials (optional) receives
- * the exact INT32 tile products as [t8][n_rows][64] (i32[pos][row][j]).
+ * the exact INT32 tile products as [t8][n_rows][64] (i32[pos][row][j]); acc_f32
+ * (optional, row stride ldo) receives the FP32 sum of the splits before the rounding,
+ * the quantity a row-parallel (K-split) sum across GPUs adds up.
  * Parallel over row tiles with OpenMP when compiled with -fopenmp. */
 void tqo_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, const int8_t* w8,
                     const float* s8, const int32_t* ids8, const int32_t* rowptr8,
                     const uint16_t* x_fp, int64_t ld_xfp, int xdtype, const uint16_t* w16,
                     const int32_t* ids16, const int32_t* rowptr16, uint16_t* out, int64_t ldo,
                     int odtype, const uint16_t* bias, int64_t n_rows, int64_t M, int64_t K,
-                    int n_tr, int n_tc, int split_k, int use_fma, int32_t* partials) {
+                    int n_tr, int n_tc, int split_k, int use_fma, int32_t* partials, float* acc_f32) {
   if (split_k < 1) split_k = 1;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int r = 0; r < n_tr; ++r) {
@@ -234,6 +236,7 @@ void tqo_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, const in
         if (col >= M) break;
         float t = acc[j];
         for (int s = 1; s < split_k; ++s) t += acc[64 * s + j];
+        if (acc_f32) acc_f32[n * ldo + col] = t;
         uint16_t y = f32_to_h(t, odtype);
         if (bias) y = f32_to_h(h_to_f32(y, odtype) + h_to_f32(bias[col], odtype), odtype);
         out[n * ldo + col] = y;

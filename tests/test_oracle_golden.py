@@ -153,3 +153,33 @@ def test_iaa_scores_match_reference(name):
 def test_topk_matches_reference(i):
     m = O.topk_mask(CALIB[f"topk{i}__imp"], float(CALIB[f"topk{i}__frac"][0]))
     np.testing.assert_array_equal(m, CALIB[f"topk{i}__mask"])
+
+
+def test_peer_sum_restatement_matches_the_gemm_on_one_rank_and_splits_exactly():
+    """The FP32 sums the oracle exposes round to its own output; a K split across two
+    'ranks' summed in rank order stays within the unsplit result's rounding."""
+    from tests.golden import inputs as I
+    from tests.helpers import assert_close_gemm
+
+    m, k, rows = 256, 512, 7
+    n_tr, n_tc = m // 64, k // 64
+    w = I.bits(I.weight(m, k, 21))
+    fp16 = I.keep_ids(n_tr, n_tc, 0.2, 22).numpy()
+    x = I.bits(I.activations(rows, k, 23))
+    q, sx = O.quantize_act(x)
+    full = O.pack(w, n_tr, n_tc, O.int8_ids_from_keep(fp16, n_tr, n_tc), fp16)
+    bias = I.bits(I.weight(1, m, 24, std=0.3)).reshape(-1)
+    want, acc = O.gemm(q, sx, full, x, m, k, bias_bits=bias, want_f32=True)
+    np.testing.assert_array_equal(O.peer_sum([acc], bias_bits=bias), want)
+    parts = []
+    for c0, c1 in ((0, 4), (4, 8)):
+        keep = np.asarray([t for t in fp16 if c0 <= t % n_tc < c1], np.int64)
+        keep = (keep // n_tc) * (c1 - c0) + keep % n_tc - c0
+        ws = np.ascontiguousarray(w[:, c0 * 64:c1 * 64])
+        pk = O.pack(ws, n_tr, c1 - c0, O.int8_ids_from_keep(keep, n_tr, c1 - c0), keep)
+        xs = np.ascontiguousarray(x[:, c0 * 64:c1 * 64])
+        qs, ss = O.quantize_act(xs)
+        np.testing.assert_array_equal(ss, sx[c0:c1])  # a column tile's scale is its own
+        parts.append(O.gemm(qs, ss, pk, xs, m, (c1 - c0) * 64, want_f32=True)[1])
+    got = O.peer_sum(parts)
+    assert_close_gemm(got, O.peer_sum([acc]), "K split over two ranks")
