@@ -68,3 +68,22 @@ def test_resolve_decision_and_keep_dirs(tmp_path):
         resolve_keep_dir(d, "keep99")
     dd, kd = resolve_decision_and_keep_dir(tmp_path / "Model-X", "gi", "keep01", tmp_path / "Decision")
     assert (dd, kd.name) == (d.resolve(), "keep01")
+
+
+def test_ensure_decision_artifacts_resolves_or_asks_for_batches(tmp_path):
+    from tilequant_b200.decisions import ensure_decision_artifacts
+
+    model_dir = tmp_path / "Model-Y"
+    model_dir.mkdir()
+    root = tmp_path / "Decision"
+    with pytest.raises(RuntimeError, match="no calibration batches"):
+        ensure_decision_artifacts(model_dir, "gi", "keep01", root)
+    d = root / "Model-Y" / "iaa"
+    (d / "tile_masks" / "keep01").mkdir(parents=True)
+    with pytest.raises(RuntimeError, match="no calibration batches"):  # IAA needs its channel statistics
+        ensure_decision_artifacts(model_dir, "iaa", "keep01", root)
+    np.savez(d / "iaa_channel_mean_abs.npz", a=np.ones(2, np.float32))
+    md, dd, kd = ensure_decision_artifacts(model_dir, "iaa", "keep01", root)
+    assert (md, dd, kd.name) == (model_dir, d.resolve(), "keep01")
+    with pytest.raises(RuntimeError, match="no calibration batches"):  # a keep dir that is not there
+        ensure_decision_artifacts(model_dir, "iaa", "keep05", root)

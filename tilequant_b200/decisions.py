@@ -201,17 +201,17 @@ def resolve_decision_and_keep_dir(local_model_dir, quant_style: str, keep_tag: O
 def load_model_and_tokenizer(model_dir, *, quant_style: str = "gi", keep_tag: Optional[str] = "keep01",
                              dtype: str = "bf16", device="cuda", iaa_channel_stats_path: Optional[str] = None,
                              decision_root="Decision", tile_m: int = 64, tile_n: int = 64,
-                             attn_implementation: Optional[str] = "sdpa"):
-    """The model of a local checkpoint with the tile maps of its existing decision
-    directory applied at load, its tokenizer, and a description (the reference's
-    application.load_model_and_tokenizer, application.py:58-139, for decision artifacts
-    that are already built; building them needs ``build_decisions_from_batches``)."""
+                             attn_implementation: Optional[str] = "sdpa", batches: Optional[Iterable] = None):
+    """The model of a local checkpoint with its tile maps applied at load, its
+    tokenizer, and a description (the reference's application.load_model_and_tokenizer,
+    application.py:58-139).  Missing decision artifacts are built first from the
+    calibration ``batches`` (``ensure_decision_artifacts``)."""
     from transformers import AutoTokenizer
 
     from .loader import ApplyConfig, TileConfig, load_mixed_precision_model_from_masks
 
-    model_dir = Path(model_dir)
-    decision_dir, keep_dir = resolve_decision_and_keep_dir(model_dir, quant_style, keep_tag, decision_root)
+    model_dir, decision_dir, keep_dir = ensure_decision_artifacts(model_dir, quant_style, keep_tag, decision_root,
+                                                                  batches=batches, device=device, dtype=dtype)
     model_type = infer_model_type(model_dir)
     quant_style = str(quant_style).lower()
     if quant_style == "iaa" and not iaa_channel_stats_path:
@@ -233,3 +233,44 @@ def load_model_and_tokenizer(model_dir, *, quant_style: str = "gi", keep_tag: Op
             "iaa_channel_stats_path": iaa_channel_stats_path, "attn_implementation": attn_implementation,
             "stats": stats}
     return model, tokenizer, info
+
+
+def ensure_decision_artifacts(model_dir, quant_style: str = "gi", keep_tag: Optional[str] = "keep01",
+                              decision_root="Decision", batches: Optional[Iterable] = None, device="cuda",
+                              dtype: str = "bf16", keep_fracs: Sequence[float] = DEFAULT_KEEP_FRACS,
+                              checkpoint_every_batches: int = 100):
+    """``(model_dir, decision_dir, keep_dir)``, building the decision directory first
+    when it, its IAA channel statistics or the requested keep directory is missing
+    (decisions.py:391-451).  Building needs calibration ``batches`` (dicts with
+    ``input_ids``; the reference draws them from its dataset instead) and runs the
+    dense checkpoint on ``device``."""
+    model_dir = Path(model_dir)
+    quant_style = str(quant_style).lower()
+    build = False
+    try:
+        decision_dir = resolve_decision_dir(model_dir, quant_style, decision_root)
+    except RuntimeError:
+        build = True
+        decision_dir = Path(decision_root).resolve() / model_dir.name / quant_style
+    if quant_style == "iaa" and not (decision_dir / "iaa_channel_mean_abs.npz").exists():
+        build = True
+    if not build:
+        try:
+            resolve_keep_dir(decision_dir, keep_tag)
+        except RuntimeError:
+            build = True
+    if build:
+        if batches is None:
+            raise RuntimeError(f"Decision artifacts missing under {decision_dir} and no calibration batches given")
+        from transformers import AutoModelForCausalLM
+
+        model = AutoModelForCausalLM.from_pretrained(str(model_dir),
+                                                     dtype=torch.float16 if dtype == "fp16" else torch.bfloat16)
+        model = model.to(torch.device(device)).eval()
+        model.config.use_cache = False
+        build_decisions_from_batches(model, batches, decision_dir, quant_style=quant_style,
+                                     model_type=infer_model_type(model_dir), model_name_or_path=str(model_dir),
+                                     keep_fracs=keep_fracs, checkpoint_every_batches=checkpoint_every_batches,
+                                     dtype=dtype)
+        del model
+    return model_dir, decision_dir, resolve_keep_dir(decision_dir, keep_tag)
