@@ -76,6 +76,9 @@ def test_other_errors_are_not_swallowed(fake_kernels):
     fake_kernels["error"] = ValueError("bias must be a contiguous [M] tensor of out_dtype")
     with pytest.raises(ValueError, match="bias"):
         mod(torch.randn(4, 128, dtype=torch.bfloat16))
+    fake_kernels["error"] = ValueError("gemm_mixed_peer_sum: peer sum: need 1 <= world <= 8 and 0 <= rank < world")
+    with pytest.raises(ValueError, match="world"):  # a misconfigured exchange is not a size fallback
+        mod(torch.randn(4, 128, dtype=torch.bfloat16))
     # a shape that worked before and then fails is an error, not a fallback
     fake_kernels["error"] = None
     mod(torch.randn(5, 128, dtype=torch.bfloat16))

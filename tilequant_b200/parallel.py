@@ -143,7 +143,9 @@ class PeerReduceSum(nn.Module):
                 self._peer_fits[rows] = True
                 return y.reshape(*x.shape[:-1], inner.M_orig)
             except (ValueError, TileQuantError) as e:
-                if "peer sum:" not in str(e) or rows in self._peer_fits:
+                too_big = any(m in str(e) for m in ("more decode CTAs than exchange slots",
+                                                    "does not fit on the GPU at once"))
+                if not too_big or rows in self._peer_fits:
                     raise
                 self._peer_fits[rows] = False  # this shape's grid does not fit: NCCL from now on
         y = inner(x)
