@@ -16,12 +16,17 @@ tiles kept BF16 (uniformly chosen), the rest INT8 with one scale per tile.
   copied back every step;
 * ``roofline`` = the dominant kernel (the stacked gate/up mixed GEMM) against the
   dense INT8 peak measured in this run (cuBLASLt INT8 8192^3 via ``torch._int_mm``);
-* ``cpu_baseline`` = the CPU restatement of the reference (oracle/, C + OpenMP) on a
-  bounded sample of the same rows.
+* ``cpu_baseline`` = the CPU restatement of the reference (oracle/, C + OpenMP on all
+  host threads) on windows of ``--cpu-rows`` consecutive rows of each linear, built
+  from the same seeded weights and tile maps, for about ``--cpu-seconds``;
+* outside the timed regions, the timed gate/up launch's output is checked against the
+  CPU restatement on rows sampled from every 128-row block; no line is printed when it
+  does not match.
 
-``--impl reference`` times that CPU restatement alone: the reference's own GEMM is a
-Triton GPU kernel that needs the reference checkout, and its CPU torch path covers
-only the quantizer and the packer.  ``--workload decode`` measures config 1 (one
+``--impl reference`` times that CPU restatement alone, one window per step, without
+loading this project's GPU library: the reference's own GEMM is a Triton GPU kernel
+whose Python sources do not travel to the GPU box, and its CPU torch path covers only
+the quantizer and the packer.  ``--workload decode`` measures config 1 (one
 q_proj-shaped MixedLinear, 16 decode tokens) in GB/s instead; ``--workload gemm``
 times one mixed GEMM launch of ``--shape`` (the case the kernel profiles capture).
 
@@ -51,6 +56,9 @@ LLAMA3B = dict(hidden=3072, inter=8192, heads=24, kv_heads=8, head_dim=128, rope
 TOKENS = (4, 2048)
 KEEP = 0.05
 METRIC_PREFILL = "tile-GEMM TOPS: Llama-3.2-3B decoder block prefill (4x2048 tokens), 4 MixedLinear forwards"
+PREFILL_CONFIG = {"workload": "config2: Llama-3.2-3B decoder block prefill", "rows": TOKENS[0] * TOKENS[1],
+                  "hidden": 3072, "intermediate": 8192, "heads": "24/8", "keep_bf16": KEEP, "tile": "64x64",
+                  "l2": "flushed (256 MB write) between timed steps"}
 GEMM_PROFILE = "umma_kernel_gate_up_8192x16384x3072.md"
 DECODE_PROFILE = "gemv_kernel_config1_16x3072x3072.md"
 
@@ -242,28 +250,112 @@ def _int8_peak(device):
         return 4500.0, f"datasheet dense INT8 (torch._int_mm failed: {type(exc).__name__})"
 
 
-def _cpu_sample(acts, block, rows):
-    """The CPU restatement of the reference (oracle/) on `rows` rows of each linear
-    input: quantize + mixed GEMM.  Returns (seconds, ops)."""
+def _bits16(t: torch.Tensor):
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view("uint16")
+
+
+def _pack_arrays(mod) -> dict:
+    """A MixedLinear's packed buffers as host arrays in the oracle's layout."""
+    pk = {}
+    for key in ("int8_tiles", "int8_scales", "int8_tile_ids", "int8_row_ptr", "fp16_tiles", "fp16_tile_ids",
+                "fp16_row_ptr"):
+        v = getattr(mod, key)
+        pk[key] = _bits16(v) if v.dtype == torch.bfloat16 else v.cpu().numpy()
+    pk.update(n_tr=mod.n_tr, n_tc=mod.n_tc)
+    return pk
+
+
+def _verify_sample(x: torch.Tensor, y: torch.Tensor, mod, seed: int = 0, per_block: int = 1) -> int:
+    """Checker (oracle/) for a full-size GEMM launch: rows sampled from every 128-row
+    token block, quantized with the scales of the whole batch, multiplied by the CPU
+    restatement and compared with the GPU output within one BF16 ulp (the tolerance of
+    tests/helpers.py).  Raises on a mismatch, so no value is printed for a kernel
+    whose output is wrong.  Returns the number of rows checked."""
+    import numpy as np
+
+    from oracle import oracle as O
+    from tests.helpers import assert_close_gemm
+
+    rows = int(x.shape[0])
+    rng = np.random.default_rng(seed)
+    sel = np.unique(np.concatenate([
+        np.minimum(rows - 1, b * 128 + rng.integers(0, 128, per_block)) for b in range((rows + 127) // 128)]))
+    xb = _bits16(x)
+    sx = O.act_scales(xb)
+    xs = np.ascontiguousarray(xb[sel])
+    ref = O.gemm(O.quantize_with_scales(xs, sx), sx, _pack_arrays(mod), xs, mod.M_orig, mod.K_orig, split_k=1,
+                 use_fma=True)
+    got = _bits16(y[torch.from_numpy(sel).to(y.device)])
+    assert_close_gemm(got, ref, f"{rows}x{mod.M_orig}x{mod.K_orig} sampled rows")
+    return int(sel.size)
+
+
+# The config-2 linears as the reference's packs: the same seeded weights and tile maps
+# as Block(seed=7) (member seeds 7 * 100 + s), Q/K/V and gate/up stacked along the
+# output rows the way concat_packs_along_rows stacks them.
+REF_LINEARS = (("qkv", ((3072, 701), (1024, 703), (1024, 705)), 3072),
+               ("o", ((3072, 707),), 3072),
+               ("gate_up", ((8192, 709), (8192, 711)), 3072),
+               ("down", ((3072, 713),), 8192))
+
+
+def _reference_linears(keep=KEEP):
+    """Host-only construction (no GPU, no tilequant_b200): oracle packs of the four
+    config-2 linears plus seeded N(0, 1) BF16 inputs of 8192 rows each."""
+    import numpy as np
+
+    from oracle import oracle as O
+    from tests.golden import inputs as I
+
+    out = []
+    for i, (name, members, k) in enumerate(REF_LINEARS):
+        n_tc = (k + 63) // 64
+        ws, keep_ids, r0 = [], [], 0
+        for m, seed in members:
+            ws.append(I.bits(I.weight(m, k, seed)))
+            keep_ids.append(I.keep_ids(m // 64, n_tc, keep, seed + 1).numpy().astype(np.int64) + r0 * n_tc)
+            r0 += m // 64
+        fp16 = np.concatenate(keep_ids)
+        w = np.concatenate(ws, axis=0)
+        pk = O.pack(w, r0, n_tc, O.int8_ids_from_keep(fp16, r0, n_tc), fp16)
+        x = I.bits(I.activations(TOKENS[0] * TOKENS[1], k, 4242 + i))
+        out.append((name, pk, x, w.shape[0], k))
+    return out
+
+
+def _cpu_sample(linears, rows: int, window: int = 0):
+    """The CPU restatement of the reference (oracle/, C + OpenMP on all host threads) on
+    one window of `rows` consecutive activation rows of each config-2 linear: quantize
+    that window (its own scales, as a call of that many rows) + mixed GEMM.  Returns
+    (seconds, ops)."""
     import numpy as np
 
     from oracle import oracle as O
 
     t_total, ops = 0.0, 0
-    for name, mod in (("x_qkv", block.qkv), ("x_o", block.o), ("x_gu", block.gate_up), ("x_down", block.down)):
-        xb = acts[name][:rows].contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
-        pk = {}
-        for key in ("int8_tiles", "int8_scales", "int8_tile_ids", "int8_row_ptr", "fp16_tiles", "fp16_tile_ids",
-                    "fp16_row_ptr"):
-            v = getattr(mod, key).cpu()
-            pk[key] = v.view(torch.int16).numpy().view(np.uint16) if v.dtype == torch.bfloat16 else v.numpy()
-        pk.update(n_tr=mod.n_tr, n_tc=mod.n_tc)
+    for _, pk, x, m, k in linears:
+        r0 = (window * rows) % max(1, x.shape[0] - rows + 1)
+        xb = np.ascontiguousarray(x[r0:r0 + rows])
         t0 = time.perf_counter()
         q, sx = O.quantize_act(xb)
-        O.gemm(q, sx, pk, xb, mod.M_orig, mod.K_orig, split_k=1)
+        O.gemm(q, sx, pk, xb, m, k, split_k=1)
         t_total += time.perf_counter() - t0
-        ops += 2 * rows * mod.M_orig * mod.K_orig
+        ops += 2 * xb.shape[0] * m * k
     return t_total, ops
+
+
+def _cpu_baseline_line(linears, rows: int, seconds: float):
+    """Windows of `rows` rows through the four linears, repeated for about `seconds`."""
+    spent, ops, w = 0.0, 0, 0
+    while spent < seconds or w < 1:
+        s, o = _cpu_sample(linears, rows, w)
+        spent += s
+        ops += o
+        w += 1
+    return {"value": ops / spent / 1e12, "unit": "TOPS", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{w} windows of {rows} consecutive rows (of 8192) through the 4 config-2 linears, each window "
+                      "quantized and multiplied as one call by oracle/tq_oracle.c (the reference's arithmetic, "
+                      "OpenMP on all host threads); weights and tile maps as the GPU run, seeded N(0,1) inputs"}
 
 
 def _prefill_setup(device):
@@ -321,19 +413,35 @@ def run_prefill(args, ws, rank, device):
     with torch.inference_mode():
         q, sx = tq.quantize_activation_tile_absmax(acts["x_gu"])
         kw = dict(x_fp=acts["x_gu"], x_int8=q, sx=sx, out_dtype=torch.bfloat16, **gu._weights())
+        y_gu = torch.empty((rows, gu.M_orig), device=device, dtype=torch.bfloat16)
         for _ in range(3):
-            tq.gemm_mixed_rows_splitk(**kw)
+            tq.gemm_mixed_rows_splitk(out=y_gu, **kw)
         kev = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(max(5, args.steps // 4))]
         for e0, e1 in kev:
             flush.zero_()
             e0.record()
-            tq.gemm_mixed_rows_splitk(**kw)
+            tq.gemm_mixed_rows_splitk(out=y_gu, **kw)
             e1.record()
         torch.cuda.synchronize()
+        # the same product as a dense BF16 cuBLAS GEMM of the unquantized weight, for context
+        w_dense = torch.randn((gu.M_orig, gu.K_orig), device=device, dtype=torch.bfloat16)
+        for _ in range(3):
+            torch.matmul(acts["x_gu"], w_dense.t())
+        dev_ = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(5)]
+        for e0, e1 in dev_:
+            flush.zero_()
+            e0.record()
+            torch.matmul(acts["x_gu"], w_dense.t())
+            e1.record()
+        torch.cuda.synchronize()
+        del w_dense
     k_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in kev)
+    bf16_ms = statistics.median(e0.elapsed_time(e1) for e0, e1 in dev_)
     k_ops = 2 * rows * gu.M_orig * gu.K_orig
     peak, peak_src = _int8_peak(device)
     achieved = k_ops / (k_ms * 1e-3) / 1e12
+    # outside the timed regions: the timed launch's output, checked on sampled rows
+    checked = _verify_sample(acts["x_gu"], y_gu, gu, seed=rank)
 
     # ---- e2e: whole block through the module API, host buffers in and out
     host_in = hidden.cpu().pin_memory()
@@ -368,14 +476,19 @@ def run_prefill(args, ws, rank, device):
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 (exact i32 tile products) + bf16, f32 accumulate",
         "data": "synthetic (seeded random init)",
-        "config": {"workload": "config2: Llama-3.2-3B decoder block prefill", "rows": rows, "hidden": 3072,
-                   "intermediate": 8192, "heads": "24/8", "keep_bf16": KEEP, "tile": "64x64",
-                   "parallelism": f"replicas x{ws}", "l2": "flushed (256 MB write) between timed steps"},
+        "config": dict(PREFILL_CONFIG, parallelism=f"replicas x{ws}"),
         "roofline": {"kernel": "mixed GEMM, stacked gate/up (8192 x 16384 x 3072)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                      "frac": round(achieved / peak, 3), "peak_source": peak_src, "ops_per_launch": k_ops,
                      "launch_ms": round(k_ms, 4), "traffic": _profile_traffic(GEMM_PROFILE),
-                     "frac_of_bf16_measured": round(achieved / _peaks().get("bf16_tflops", 1639.7), 3)},
+                     "traffic_source": f"static: ncu capture summarised in profiles/{GEMM_PROFILE}",
+                     "bf16_dense_ms": round(bf16_ms, 4),
+                     "bf16_dense_what": "torch.matmul (cuBLAS) of the same activations by a dense BF16 weight "
+                                        "of the same shape",
+                     "frac_of_bf16_measured": round(achieved / _peaks().get("bf16_tflops", 1639.7), 3),
+                     "checked_rows": checked,
+                     "check": "output of the timed launch on sampled rows (every 128-row block) against the "
+                              "CPU restatement (oracle/), within 1 BF16 ulp"},
         "e2e": {"value": round(ws * ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
                 "h2d_bytes_per_step": hidden.numel() * 2, "d2h_bytes_per_step": hidden.numel() * 2,
                 "what": "whole decoder block through MixedLinear modules, pinned host in/out"},
@@ -383,12 +496,8 @@ def run_prefill(args, ws, rank, device):
         "clocks": clocks.summary(),
         "block_ms": round(block_ms, 4),
     }
-    if rank == 0:
-        secs, cops = _cpu_sample(acts, block, args.cpu_rows)
-        line["cpu_baseline"] = {"value": cops / secs / 1e12, "unit": "TOPS", "cores": os.cpu_count() or 1,
-                                "kind": "port",
-                                "sample": f"{args.cpu_rows} of 8192 rows through the 4 linears "
-                                          "(oracle/tq_oracle.c restatement of the reference, OpenMP)"}
+    if rank == 0 and ws == 1:
+        line["cpu_baseline"] = _cpu_baseline_line(_reference_linears(), args.cpu_rows, args.cpu_seconds)
     return line
 
 
@@ -704,32 +813,36 @@ def run_generate(args, ws, rank, device):
 
 
 def run_reference(args, ws, rank):
-    """CPU restatement of the reference (oracle/) on a bounded sample of config 2."""
+    """The reference arm: the reference's arithmetic on the host cores (the C
+    restatement in oracle/, all host threads), on config 2.  The reference's own GEMM
+    is a Triton GPU kernel and its Python sources do not travel to the GPU box, so the
+    restatement stands in for it.  Nothing here loads this project's GPU library or
+    touches a GPU: the packs are built by the restatement from the same seeded weights
+    and tile maps as the GPU run.  Each step is one window of --cpu-rows consecutive
+    rows of each linear's 8192-row input (the windows walk through the batch),
+    quantized and multiplied as one call."""
     if rank != 0:
         return None
-    if not torch.cuda.is_available():
-        return {"impl": "reference", "unavailable": "no CUDA device to pack the workload's weights"}
-    device = torch.device("cuda", 0)
-    block, hidden, acts, rows = _prefill_setup(device)
-    for _ in range(args.warmup):
-        _cpu_sample(acts, block, args.cpu_rows)
+    linears = _reference_linears()
+    for w in range(args.warmup):
+        _cpu_sample(linears, args.cpu_rows, w)
     secs, ops = 0.0, 0
-    for _ in range(args.steps):
-        s, o = _cpu_sample(acts, block, args.cpu_rows)
+    for i in range(args.steps):
+        s, o = _cpu_sample(linears, args.cpu_rows, args.warmup + i)
         secs += s
         ops += o
     value = ops / secs / 1e12
     threads = os.cpu_count() or 1
+    sample = (f"per step one window of {args.cpu_rows} consecutive rows (of 8192) through the 4 config-2 linears, "
+              "quantized and multiplied as one call by oracle/tq_oracle.c (OpenMP, all host threads); weights and "
+              "tile maps as the GPU run (same seeds), seeded N(0,1) inputs")
     return {
         "impl": "reference", "metric": METRIC_PREFILL, "value": value, "unit": "TOPS", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16 (CPU)",
         "data": "synthetic (seeded random init)",
-        "config": {"workload": "config2: Llama-3.2-3B decoder block prefill",
-                   "rows_sampled_per_linear": args.cpu_rows},
-        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port",
-                         "sample": f"{args.cpu_rows} of 8192 rows through the 4 linears per step "
-                                   "(oracle/tq_oracle.c, OpenMP)"},
+        "config": dict(PREFILL_CONFIG, parallelism="one host, all cores"),
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -747,7 +860,8 @@ def main():
                     help="--tp: row-parallel sums of decode calls inside the GEMM (peer) or by NCCL")
     ap.add_argument("--shape", default="8192x16384x3072", help="ROWSxMxK of --workload gemm")
     ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
-    ap.add_argument("--cpu-rows", type=int, default=8, help="rows per linear in the CPU baseline sample")
+    ap.add_argument("--cpu-rows", type=int, default=256, help="rows per linear in one CPU window")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline leg: seconds of windows")
     args = ap.parse_args()
     ws, rank, local = _dist()
     if args.impl == "reference":

@@ -226,14 +226,16 @@ TQ_API int tq_gemm_mixed_peer_sum(const int8_t* x_i8, int64_t ld_x8, const float
  * exchange-address table live in one file-scope __device__ array of
  * TQ_NOALLOC_SCRATCH_BYTES (about 4 MB) that every GPU loading the library holds until
  * the process exits.  A world of one GPU (the current device): that array cannot be
- * reached from other GPUs, so sums across GPUs need tq_peer_alloc's buffers.  1..16
- * rows and m <= 16384 (256 row tiles, 1024 CTA slots); larger requests are rejected
- * (TQ_ERR_INVALID) before anything runs.  The first call on a device looks up the
- * array's address and writes its table with a synchronous copy, so make it before any
- * stream capture.  Every call shares the array, which keeps the last call's state (the
- * call counters advance; each call's words carry its number, so nothing needs clearing
+ * reached from other GPUs, so sums across GPUs need tq_peer_alloc's buffers.  Limits,
+ * checked before anything runs: more than 16 rows returns TQ_ERR_UNSUPPORTED (not a
+ * decode call), m > 16384 (more than 256 row tiles, beyond the array's 1024 CTA slots)
+ * returns TQ_ERR_INVALID.  Every call looks up the array's address; the first call on a
+ * device writes the array's table with a synchronous copy, so make it before any stream
+ * capture.  Every call shares the array, which keeps the last call's state (the call
+ * counters advance; each call's words carry its number, so nothing needs clearing
  * between calls): calls whose kernels overlap on the GPU race.  reset_only != 0 zeroes
- * the counters and words (e.g. after a timeout) and launches nothing.  Otherwise the
+ * the counters and words and rewrites the table (stream-ordered, no launch): use it
+ * after a timeout, and after a cudaDeviceReset before the next call.  Otherwise the
  * contract and the result of tq_gemm_mixed_peer_sum with world 1 (the same bits as
  * tq_gemm_mixed on the decode kernel). */
 #define TQ_NOALLOC_SLOTS 1024

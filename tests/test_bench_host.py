@@ -27,3 +27,15 @@ def test_bench_help_lists_the_workloads():
         assert flag in out
     for workload in ("prefill", "decode", "gemm", "generate"):
         assert workload in out
+
+
+def test_reference_arm_is_host_only():
+    """The reference arm times the CPU restatement without this project's GPU library."""
+    code = ("import sys, types, bench; "
+            "a = types.SimpleNamespace(steps=1, warmup=0, cpu_rows=4); "
+            "line = bench.run_reference(a, 1, 0); "
+            "assert line['impl'] == 'reference' and line['value'] > 0, line; "
+            "assert line['config'] == dict(bench.PREFILL_CONFIG, parallelism='one host, all cores'); "
+            "assert 'tilequant_b200' not in sys.modules, 'GPU library imported'; print('ok')")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=ROOT, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]

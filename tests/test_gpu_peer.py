@@ -166,3 +166,4 @@ def test_peer_sum_host_side_rejections(cuda_device):
         PeerExchange(DEV, world=9, rank=0)
     with pytest.raises(ValueError):
         PeerExchange(DEV, world=2, rank=2)
+

@@ -93,3 +93,78 @@ def test_umma_bias_and_ragged_rows(cuda_device):
 def test_auto_picks_tcgen05_for_prefill(cuda_device):
     x, p, pk = _case(512, 256, 512, 0.05, 900)
     assert torch.equal(_run(x, p, 256, 512, algo=0), _run(x, p, 256, 512, algo=UMMA))
+
+
+# ------------------------------------------------------------------ multi-wave cases
+# The kernel is persistent (one CTA per SM, 148 on a B200) and walks output tiles of
+# 128 activation rows x 128 output columns; the cases below hold two to seven times as
+# many tiles as CTAs, so every CTA reuses its column-table ring slots, its TMEM groups
+# and its barrier phases across tiles.
+
+def _tiles(rows, m):
+    return ((rows + 127) // 128) * ((m + 127) // 128)
+
+
+@pytest.mark.parametrize("rows,m,k", [(2048, 2560, 512), (4096, 4096, 256)])
+def test_umma_multiwave_int8_only_bit_exact(cuda_device, rows, m, k):
+    assert _tiles(rows, m) > 2 * 148
+    x, p, pk = _case(rows, m, k, 0.0, 1100 + rows)
+    y = from_torch16(_run(x, p, m, k))
+    q, sx = O.quantize_act(I.bits(x))
+    ref = O.gemm(q, sx, pk, I.bits(x), m, k, split_k=1, use_fma=True)
+    np.testing.assert_array_equal(y, ref)
+
+
+def test_umma_multiwave_ragged_mixed_within_one_ulp(cuda_device):
+    """1500 rows (a partial last token block), 2240 = 35 row tiles (an odd count: the
+    last output tile has one row tile), 576 = 9 column tiles, 10 % 16-bit tiles."""
+    rows, m, k = 1500, 2240, 576
+    assert _tiles(rows, m) > 148
+    x, p, pk = _case(rows, m, k, 0.1, 1200)
+    y = from_torch16(_run(x, p, m, k))
+    q, sx = O.quantize_act(I.bits(x))
+    ref = O.gemm(q, sx, pk, I.bits(x), m, k, split_k=1, use_fma=True)
+    assert_close_gemm(y, ref, "ragged multi-wave")
+    assert (ulp_dist16(y, ref) == 0).mean() > 0.98
+
+
+def test_umma_multiwave_partials_bit_exact(cuda_device):
+    rows, m, k = 2048, 2560, 512
+    x, p, pk = _case(rows, m, k, 0.1, 1300)
+    q, sx = tq.quantize_activation_tile_absmax(x.to(DEV))
+    parts = tq.gemm_int8_partials(x_int8=q, int8_tiles=p.int8_tiles, int8_tile_ids=p.int8_tile_ids,
+                                  int8_row_ptr=p.int8_row_ptr, K=k, n_tr=p.n_tr, n_tc=p.n_tc, algo=UMMA)
+    _, ref = O.gemm(q.cpu().numpy(), sx.cpu().numpy(), pk, I.bits(x), m, k, want_partials=True)
+    np.testing.assert_array_equal(parts.cpu().numpy(), ref)
+
+
+# ------------------------------------------------- the shapes bench.py times (config 2)
+# One Llama-3.2-3B block at prefill: 8192 activation rows, 5 % 16-bit tiles.  Output
+# rows are independent once the activation scales are fixed, so the oracle checks a
+# sample of rows (one in every 128-row token block, at a different lane each time) of
+# the full-size launch, with the scales of the whole batch.
+
+CONFIG2 = {"qkv": (5120, 3072), "o": (3072, 3072), "gate_up": (16384, 3072), "down": (3072, 8192)}
+
+
+def sample_rows(rows: int, seed: int = 0) -> np.ndarray:
+    blocks = (rows + 127) // 128
+    rng = np.random.default_rng(seed)
+    return np.array([min(rows - 1, b * 128 + int(rng.integers(0, 128))) for b in range(blocks)], np.int64)
+
+
+@pytest.mark.parametrize("name", sorted(CONFIG2))
+def test_umma_config2_shapes_sampled_rows(cuda_device, name):
+    m, k = CONFIG2[name]
+    rows = 8192
+    x, p, pk = _case(rows, m, k, 0.05, 1400 + m + k)
+    y = _run(x, p, m, k)
+    sel = sample_rows(rows, seed=m + k)
+    y_s = from_torch16(y[torch.from_numpy(sel).to(DEV)])
+    xb = I.bits(x)
+    sx = O.act_scales(xb)  # scales of the whole batch
+    xs = np.ascontiguousarray(xb[sel])
+    q = O.quantize_with_scales(xs, sx)
+    ref = O.gemm(q, sx, pk, xs, m, k, split_k=1, use_fma=True)
+    assert_close_gemm(y_s, ref, f"{name} {rows}x{m}x{k}")
+    assert (ulp_dist16(y_s, ref) == 0).mean() > 0.98

@@ -86,3 +86,25 @@ def test_other_errors_are_not_swallowed(fake_kernels):
                                              "does not fit on the GPU at once")
     with pytest.raises(N.TileQuantError):
         mod(torch.randn(5, 128, dtype=torch.bfloat16))
+
+
+def test_decoder_peer_status_raises_after_a_timeout():
+    """The decoder's synchronised points read the exchanges' error words: a peer sum that
+    gave up waiting surfaces as TileQuantError instead of silently wrong tokens."""
+    from tilequant_b200 import _native as N
+    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
+
+    class Exchange:  # the error word of a PeerExchange, as status() reads it
+        def __init__(self):
+            self.word = N.TQ_OK
+
+        def status(self):
+            return self.word
+
+    ex = Exchange()
+    dec = CudaGraphGreedyDecoder.__new__(CudaGraphGreedyDecoder)
+    dec._exchanges = [ex]
+    dec.check_peer_status()
+    ex.word = N.TQ_ERR_TIMEOUT
+    with pytest.raises(N.TileQuantError, match="reset the exchange"):
+        dec.check_peer_status()

@@ -13,14 +13,17 @@
 // same process faulted on it here even with peer access enabled), so the sums across
 // GPUs stay with tq_gemm_mixed_peer_sum and its tq_peer_alloc buffers.
 //
-// Set-up, once per device and with that device current: the array's device address
-// (cudaGetSymbolAddress; in host code the array's name only stands for it) and the
-// table entry, written with a synchronous copy -- so the first call on a device does
-// that work and should come before any stream capture.  Every call shares the array and
-// it keeps the last call's state (the counters advance call by call; the exchange words
-// of a call carry its number, so nothing has to be cleared between calls), so calls
-// whose kernels overlap on one GPU race.  reset_only zeroes the array again (e.g. after
-// a timeout) without a launch.
+// Set-up, per device and with that device current: the array's device address
+// (cudaGetSymbolAddress; in host code the array's name only stands for it) is looked up
+// on every call, which is cheap, and the table entry that holds it is written with a
+// synchronous copy whenever that address is new for the device -- so the first call on
+// a device does that copy and should come before any stream capture.  Every call shares
+// the array and it keeps the last call's state (the counters advance call by call; the
+// exchange words of a call carry its number, so nothing has to be cleared between
+// calls), so calls whose kernels overlap on one GPU race.  reset_only zeroes the
+// counters and words again and rewrites the table entry, without a launch: use it after
+// a timeout, and after a cudaDeviceReset (which reloads the array as zeros, possibly at
+// the same address) before the next call.
 #include <mutex>
 
 #include "common.cuh"
@@ -45,20 +48,21 @@ constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned char* g_addr[kMaxDevices] = {};  // device address of the scratch, per device
 
-// Set-up of the current device `dev`: the scratch's address and its table entry.
+// The scratch's address on the current device `dev`; the table entry is (re)written
+// when the address differs from the one recorded for the device.
 int scratch_of(int dev, unsigned char** out) {
   if (dev < 0 || dev >= kMaxDevices) return tq_set_error(TQ_ERR_INVALID, "no-alloc peer sum: device ordinal out of range");
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, tq_noalloc_scratch) != cudaSuccess || !p)
+    return tq_set_error(TQ_ERR_CUDA, "no-alloc peer sum: cudaGetSymbolAddress of the scratch array failed");
+  unsigned char* base = static_cast<unsigned char*>(p);
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, tq_noalloc_scratch) != cudaSuccess || !p)
-      return tq_set_error(TQ_ERR_CUDA, "no-alloc peer sum: cudaGetSymbolAddress of the scratch array failed");
-    unsigned char* base = static_cast<unsigned char*>(p);
+  if (g_addr[dev] != base) {
     float* words = reinterpret_cast<float*>(base + kWordsOff);
     TQ_CUDA_TRY(cudaMemcpy(base + kTableOff, &words, sizeof(words), cudaMemcpyHostToDevice));
     g_addr[dev] = base;
   }
-  *out = g_addr[dev];
+  *out = base;
   return TQ_OK;
 }
 }  // namespace
@@ -74,7 +78,10 @@ extern "C" int tq_gemm_mixed_peer_sum_noalloc(
   unsigned char* base = nullptr;
   const int rc = scratch_of(dev, &base);
   if (rc) return rc;
-  if (reset_only) {  // back to the state at load: counters and words zero, the table kept
+  if (reset_only) {  // counters and words zero, the table entry rewritten (stream-ordered)
+    float* words = reinterpret_cast<float*>(base + kWordsOff);
+    TQ_CUDA_TRY(cudaMemcpyAsync(base + kTableOff, &words, sizeof(words), cudaMemcpyHostToDevice,
+                                (cudaStream_t)stream));
     TQ_CUDA_TRY(cudaMemsetAsync(base + kCountOff, 0, kBytes - kCountOff, (cudaStream_t)stream));
     return TQ_OK;
   }

@@ -138,6 +138,10 @@ class CudaGraphGreedyDecoder:
         self.prefill_captured = False
         # kernels of this library in one replay of each graph (counted during capture)
         self.captured_launches = {"prefill": 0, "decode": 0}
+        # peer-sum exchanges of tensor-parallel row-parallel projections: their error
+        # words are read at the synchronised points (check_peer_status)
+        self._exchanges = list({id(ex): ex for ex in (getattr(m, "exchange", None) for m in model.modules())
+                                if ex is not None and hasattr(ex, "status")}.values())
         self._prepared = False
         self._attach()
 
@@ -328,4 +332,18 @@ class CudaGraphGreedyDecoder:
         ids = self.decode(new_tokens - 1)
         torch.cuda.synchronize(self.device)
         end = time.perf_counter()
+        self.check_peer_status()
         return ids, GreedyGenerationTiming(start, first, end)
+
+    def check_peer_status(self) -> None:
+        """Raise ``TileQuantError`` if a row-parallel peer sum of the model gave up
+        waiting for a peer (its outputs, and so the generated ids, are then undefined;
+        every rank must reset its exchange before the next request).  Reads each
+        exchange's error word, which synchronises; no-op without exchanges."""
+        from ._native import TQ_OK, TileQuantError
+
+        for ex in self._exchanges:
+            st = ex.status()
+            if st != TQ_OK:
+                raise TileQuantError(f"peer sum: a wait for a peer rank ran out (status {st}); reset the exchange "
+                                     "on every rank before the next request")
