@@ -108,6 +108,42 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait that lets the waiting warp sleep instead of spinning: a few plain polls,
+// then polls that suspend the thread until the phase completes or `kSleepNs` passes,
+// so waiting warps take almost no issue slots from the warps doing the work.  Gives up
+// (TQ_ERR_TIMEOUT) after about two seconds.
+constexpr uint32_t kSleepNs = 20000;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err) {
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, kSleepNs)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
+  }
+  report(err, TQ_ERR_TIMEOUT);
+  return false;
+}
+
 // 1-D bulk copy global -> shared (TMA engine), completion counted on `bar`.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -27,7 +27,7 @@
 //               and combined scale sx*sw of the RT row tiles at every column, 16-bit tile
 //               columns) one tile ahead into a 2-slot ring, so no role stalls on the
 //               id lists;
-//   warp 3      idle (completes warpgroup 0, which gives registers to the epilogue);
+//   warp 3      second TMA producer (the other half of the weight tiles);
 //   warps 4-11  epilogue: two per TMEM lane quadrant, each over half of the step's
 //               columns.  Every K step's first MMA overwrites its INT32 TMEM tile (the
 //               second accumulates), so each word read back is that step's tile dot; it
@@ -129,6 +129,13 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
   }
+}
+
+// One lane of the (converged) warp, chosen by the hardware.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n" : "=r"(pred));
+  return pred != 0;
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
 
   if (tid == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 2);  // the two producers
       mbar_init(&sempty[i], 1);
     }
     for (int b = 0; b < NG; ++b) {
@@ -259,7 +266,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&qfull[s], 32);
-      mbar_init(&qempty[s], 3);
+      mbar_init(&qempty[s], 4);  // two producers, MMA issuer, epilogue
     }
     fence_mbar_init();
   }
@@ -294,7 +301,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
       uint32_t k = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
         const int slot = k & 1;
-        if (ok && !mbar_wait_bounded(&qempty[slot], ((k >> 1) & 1) ^ 1, a.err)) ok = false;
+        if (ok && !mbar_wait_sleep(&qempty[slot], ((k >> 1) & 1) ^ 1, a.err)) ok = false;
         TileHdr* h = t_hdr(slot);
         int* pos = t_pos(slot);
         float* scl = t_scl(slot);
@@ -336,57 +343,73 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
         __syncwarp();
         mbar_arrive(&qfull[slot]);  // every lane publishes its writes
       }
-    } else if (warp == 0) {
-      // ================================================================ TMA producer
-      if (lane == 0) {
-        uint32_t g = 0, k = 0;
-        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
-          const int slot = k & 1;
-          if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
-          const TileHdr* h = t_hdr(slot);
-          const int tb = h->tb, n_r = h->n_r;
-          const int* pos = t_pos(slot);
-          const int* bcol = t_bcol(slot);
-          for (int c0 = 0; c0 < n_tc; c0 += GS, ++g) {  // GS INT8 K steps per stage
-            const int stg = g % NS, ns = min(GS, n_tc - c0);
-            if (ok && !mbar_wait_bounded(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
-            mbar_expect_tx(&full[stg], ns * STEP_BYTES);
+    } else if (warp == 0 || warp == 3) {
+      // ================================================================ TMA producers
+      // P0 (warp 0): the activation box and the first half of the row tiles' weight
+      // tiles of every K step, and the 16-bit tiles; P1 (warp 3): the other half of the
+      // weight tiles.  Both arrive on every stage's full barrier.  The whole warp runs the
+      // loop (warp-uniform control flow keeps the TMA operands in uniform registers, which
+      // more than halves the cost of issuing a box); one elected lane issues.
+      const bool leader = elect_one();
+      const bool p0 = warp == 0;
+      const int j_lo = p0 ? 0 : RT / 2, j_hi = p0 ? RT / 2 : RT;
+      const uint32_t step_bytes = (p0 ? A_BYTES : 0) + (j_hi - j_lo) * W_BYTES;
+      uint32_t g = 0, k = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
+        const int slot = k & 1;
+        if (ok && !mbar_wait_sleep(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
+        const TileHdr* h = t_hdr(slot);
+        const int tb = h->tb, n_r = h->n_r;
+        const int* pos = t_pos(slot);
+        const int* bcol = t_bcol(slot);
+        for (int c0 = 0; c0 < n_tc; c0 += GS, ++g) {  // GS INT8 K steps per stage
+          const int stg = g % NS, ns = min(GS, n_tc - c0);
+          if (ok && !mbar_wait_sleep(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
+          if (leader) {
+            mbar_expect_tx(&full[stg], ns * step_bytes);
             for (int s = 0; s < ns; ++s) {
               const int c = c0 + s;
               uint8_t* sa = stages + stg * STAGE + s * STEP_BYTES;
-              tma_load_2d(sa, &maps.x8, c * 64, tb * BM, &full[stg]);
-  #pragma unroll
-              for (int j = 0; j < RT; ++j) {
+              if (p0) tma_load_2d(sa, &maps.x8, c * 64, tb * BM, &full[stg]);
+              for (int j = j_lo; j < j_hi; ++j) {
                 const int p = pos[j * n_tc + c];
                 tma_load_2d(sa + A_BYTES + j * W_BYTES, &maps.w8, 0, p >= 0 ? p * 64 : oob_row, &full[stg]);
               }
             }
           }
-          for (int j = 0; j < n_r; ++j) {  // one 16-bit tile (two 32-column halves) per stage
-            const int n16 = h->n16[j], b16 = h->b16[j];
-            for (int i = 0; i < n16; ++i, ++g) {
-              const int stg = g % NS;
-              if (ok && !mbar_wait_bounded(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
-              const int c = bcol[j * n_tc + i];
-              mbar_expect_tx(&full[stg], 2 * (A_BYTES + W_BYTES));
-              for (int half = 0; half < 2; ++half) {
-                uint8_t* sa = stages + stg * STAGE + half * (A_BYTES + W_BYTES);
-                tma_load_2d(sa, &maps.xfp, c * 64 + half * 32, tb * BM, &full[stg]);
-                tma_load_2d(sa + A_BYTES, &maps.w16, half * 32, (b16 + i) * 64, &full[stg]);
-              }
+        }
+        for (int j = 0; j < n_r; ++j) {  // one 16-bit tile (two 32-column halves) per stage
+          const int n16 = h->n16[j], b16 = h->b16[j];
+          for (int i = 0; i < n16; ++i, ++g) {
+            const int stg = g % NS;
+            if (ok && !mbar_wait_sleep(&sempty[stg], ((g / NS) & 1) ^ 1, a.err)) ok = false;
+            if (!leader) continue;
+            if (!p0) {
+              mbar_arrive(&full[stg]);
+              continue;
+            }
+            const int c = bcol[j * n_tc + i];
+            mbar_expect_tx(&full[stg], 2 * (A_BYTES + W_BYTES));
+            for (int half = 0; half < 2; ++half) {
+              uint8_t* sa = stages + stg * STAGE + half * (A_BYTES + W_BYTES);
+              tma_load_2d(sa, &maps.xfp, c * 64 + half * 32, tb * BM, &full[stg]);
+              tma_load_2d(sa + A_BYTES, &maps.w16, half * 32, (b16 + i) * 64, &full[stg]);
             }
           }
-          mbar_arrive(&qempty[slot]);
         }
+        __syncwarp();
+        if (leader) mbar_arrive(&qempty[slot]);
       }
     } else if (warp == 1) {
       // ================================================================ MMA issuer
-      if (lane == 0) {
+      // The whole warp runs the loop; one elected lane issues the tcgen05 instructions.
+      {
+        const bool leader = elect_one();
         uint32_t g = 0, k = 0, grp = 0;
         const uint32_t idesc16 = XT == TQ_DTYPE_BF16 ? IDESC_BF16 : IDESC_F16;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
           const int slot = k & 1;
-          if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
+          if (ok && !mbar_wait_sleep(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
           const TileHdr* h = t_hdr(slot);
           const int n_r = h->n_r;
           int n16s[RT];
@@ -396,47 +419,53 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
             n16s[j] = h->n16[j];
             n16_all += n16s[j];
           }
-          mbar_arrive(&qempty[slot]);  // only the header was needed
+          if (leader) mbar_arrive(&qempty[slot]);  // only the header was needed
           for (int c0 = 0; c0 < n_tc; c0 += GS, ++g, ++grp) {
             const int stg = g % NS, ns = min(GS, n_tc - c0);
             const uint32_t gb = grp % NG;
-            if (ok && !mbar_wait_bounded(&full[stg], (g / NS) & 1, a.err)) ok = false;
-            if (ok && !mbar_wait_bounded(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait_sleep(&full[stg], (g / NS) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait_sleep(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
             tc_fence_after();
             for (int s = 0; s < ns; ++s) {
               const uint32_t sa = smem_u32(stages + stg * STAGE + s * STEP_BYTES);
               const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
               const uint32_t d = tmem + (gb * GS + s) * BN;
               // the first K half overwrites the step buffer, the second accumulates
-              umma(d, da, db, G::IDESC, 0, true);
-              umma(d, da + 2, db + 2, G::IDESC, 1, true);
+              if (leader) {
+                umma(d, da, db, G::IDESC, 0, true);
+                umma(d, da + 2, db + 2, G::IDESC, 1, true);
+              }
             }
-            umma_commit(&sempty[stg]);
-            umma_commit(&tfull[gb]);
+            if (leader) {
+              umma_commit(&sempty[stg]);
+              umma_commit(&tfull[gb]);
+            }
           }
           if (n16_all > 0) {  // the 16-bit tiles: one more group, first buffer only
             const uint32_t gb = grp % NG;
-            if (ok && !mbar_wait_bounded(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait_sleep(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
             tc_fence_after();
   #pragma unroll
             for (int j = 0; j < RT; ++j) {
               const int n16 = j < n_r ? n16s[j] : 0;
               for (int i = 0; i < n16; ++i, ++g) {
                 const int stg = g % NS;
-                if (ok && !mbar_wait_bounded(&full[stg], (g / NS) & 1, a.err)) ok = false;
+                if (ok && !mbar_wait_sleep(&full[stg], (g / NS) & 1, a.err)) ok = false;
                 tc_fence_after();
                 for (int half = 0; half < 2; ++half) {
                   const uint32_t sa = smem_u32(stages + stg * STAGE + half * (A_BYTES + W_BYTES));
                   const uint64_t da = sw64_desc(sa), db = sw64_desc(sa + A_BYTES);
                   const uint32_t d = tmem + gb * GS * BN + j * 64;
                   // the first MMA of a row tile overwrites the buffer
-                  umma(d, da, db, idesc16, (i == 0 && half == 0) ? 0 : 1, false);
-                  umma(d, da + 2, db + 2, idesc16, 1, false);
+                  if (leader) {
+                    umma(d, da, db, idesc16, (i == 0 && half == 0) ? 0 : 1, false);
+                    umma(d, da + 2, db + 2, idesc16, 1, false);
+                  }
                 }
-                umma_commit(&sempty[stg]);
+                if (leader) umma_commit(&sempty[stg]);
               }
             }
-            umma_commit(&tfull[gb]);
+            if (leader) umma_commit(&tfull[gb]);
             ++grp;
           }
         }
@@ -458,7 +487,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
     uint32_t k = 0, grp = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++k) {
       const int slot = k & 1;
-      if (ok && !mbar_wait_bounded(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
+      if (ok && !mbar_wait_sleep(&qfull[slot], (k >> 1) & 1, a.err)) ok = false;
       const TileHdr* h = t_hdr(slot);
       const float* scl = t_scl(slot) + j0 * n_tc;
       const int* pos = t_pos(slot) + j0 * n_tc;
@@ -484,7 +513,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
             pp[s][t] = DUMP && in ? pos[t * n_tc + c0 + s] : -1;
           }
         const uint32_t t0 = tbase + gb * GS * BN;  // step s, chunk u at t0 + s * BN + u * CH
-        if (ok && !mbar_wait_bounded(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
+        if (ok && !mbar_wait_sleep(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
         tc_fence_after();
         // CH-column chunks (step s = i / CPS, columns CH * (i % CPS)), each chunk's load
         // issued before the previous chunk's rescale so the TMEM latency overlaps FP work
@@ -513,7 +542,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
       for (int jj = 0; jj < RT; ++jj) n16_all += h->n16[jj];
       if (n16_all > 0) {
         const uint32_t gb = grp % NG;
-        if (ok && !mbar_wait_bounded(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
+        if (ok && !mbar_wait_sleep(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
         tc_fence_after();
 #pragma unroll
         for (int t = 0; t < NJ; ++t) {

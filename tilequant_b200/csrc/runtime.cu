@@ -60,8 +60,7 @@ extern "C" const char* tq_status_string(int status) {
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-int tq_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t cols,
-                 uint64_t rows, uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+static int load_encoder() {
   if (!g_encode) {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -70,6 +69,28 @@ int tq_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, co
       return tq_set_error(TQ_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
     g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
+  return TQ_OK;
+}
+
+int tq_encode_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
+                    uint64_t stride2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle swizzle) {
+  if (load_encoder() != TQ_OK) return TQ_ERR_UNSUPPORTED;
+  if (((uintptr_t)base & 15) || (stride1 & 15) || (stride2 & 15) || !d0 || !d1 || !d2)
+    return tq_set_error(TQ_ERR_UNSUPPORTED, "tensor map needs 16-byte aligned base and strides");
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1, stride2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return tq_set_error(TQ_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled rejected the 3-D layout");
+  return TQ_OK;
+}
+
+int tq_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, uint64_t cols,
+                 uint64_t rows, uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  if (load_encoder() != TQ_OK) return TQ_ERR_UNSUPPORTED;
   if (((uintptr_t)base & 15) || (ld_bytes & 15) || rows == 0 || cols == 0)
     return tq_set_error(TQ_ERR_UNSUPPORTED, "tensor map needs 16-byte aligned base and row stride");
   cuuint64_t dims[2] = {cols, rows};
