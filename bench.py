@@ -30,8 +30,14 @@ the quantizer and the packer.  ``--workload decode`` measures config 1 (one
 q_proj-shaped MixedLinear, 16 decode tokens) in GB/s instead; ``--workload gemm``
 times one mixed GEMM launch of ``--shape`` (the case the kernel profiles capture).
 
-Multi-GPU (torchrun): every rank runs its own replica of the workload (weak scaling);
-the step time is the max over ranks.
+The default line also carries ``decode`` (config 1: decode GEMM GB/s, fraction of HBM)
+and ``generate`` (config 3: decode tokens/s, p50 TTFT and TPOT) sub-objects.
+
+Multi-GPU (torchrun): the default workload is strong-scaled by tensor parallelism (the
+same block and total work at every N: Q/K/V and gate/up column-parallel, O and down
+row-parallel with an NCCL all-reduce of their partial outputs); the step time is the
+max over ranks.  ``--workload decode``/``gemm`` run one replica per rank (weak scaling),
+``--workload generate --tp`` shards the model over the ranks.
 """
 
 from __future__ import annotations
@@ -369,6 +375,143 @@ def _prefill_setup(device):
         block.forward(hidden, capture=acts)
     torch.cuda.synchronize()
     return block, hidden, acts, rows
+
+
+def _mixed_linear_shard(out_f, in_f, seed, device, rows=None, cols=None, keep=KEEP):
+    """This rank's slice of the config-2 linear `_mixed_linear(out_f, in_f, seed)` makes:
+    output features `rows` = [r0, r1) and input features `cols` = [c0, c1) (64-aligned)
+    of the same seeded weight, packed with the full tile map restricted to the slice (so
+    its tiles and scales are the single-GPU pack's)."""
+    import tilequant_b200 as tq
+    from tests.golden import inputs as I
+    from tilequant_b200.parallel import restrict_keep_ids
+
+    w = I.weight(out_f, in_f, seed)
+    n_tr, n_tc = (out_f + 63) // 64, (in_f + 63) // 64
+    keep_full = I.keep_ids(n_tr, n_tc, keep, seed + 1)
+    r0, r1 = rows if rows is not None else (0, out_f)
+    c0, c1 = cols if cols is not None else (0, in_f)
+    keep_ids, s_tr, s_tc = restrict_keep_ids(keep_full, n_tc, rows=(r0 // 64, (r1 + 63) // 64),
+                                             cols=(c0 // 64, (c1 + 63) // 64))
+    ws_ = w[r0:r1, c0:c1].contiguous().to(device)
+    pack = tq.pack_weight_from_tile_ids(ws_, n_tr=s_tr, n_tc=s_tc, int8_tile_ids=I.complement_ids(keep_ids, s_tr * s_tc),
+                                        fp16_tile_ids=keep_ids, cfg=_cfg())
+    return tq.MixedLinear(pack, None, _cfg())
+
+
+class BlockShard:
+    """Rank `rank`'s tensor-parallel shard of Block(seed=7)'s four linears over `world`
+    ranks: Q/K/V (this rank's heads) and gate/up (its intermediate row tiles)
+    column-parallel, O and down row-parallel over the same head / intermediate ranges."""
+
+    def __init__(self, rank, world, device, seed=7, dims=LLAMA3B):
+        import tilequant_b200 as tq
+        from tilequant_b200.parallel import head_shard, split_range
+
+        h, i, nh, nkv, hd = dims["hidden"], dims["inter"], dims["heads"], dims["kv_heads"], dims["head_dim"]
+        hs = head_shard(nh, nkv, rank, world)
+        (q0, q1), (k0, k1) = hs.q_heads, hs.kv_heads
+        t0, t1 = split_range(i // 64, world, rank)
+        self.q_cols = (q0 * hd, q1 * hd)   # this rank's attention-output columns (O's input)
+        self.i_cols = (t0 * 64, t1 * 64)   # this rank's intermediate features (down's input)
+        sd = seed * 100
+        lin = lambda o, k, s, rows=None, cols=None: _mixed_linear_shard(o, k, sd + s, device, rows, cols)  # noqa: E731
+        self.qkv = tq.MixedLinearGroup([lin(nh * hd, h, 1, rows=self.q_cols), lin(nkv * hd, h, 3, rows=(k0 * hd, k1 * hd)),
+                                        lin(nkv * hd, h, 5, rows=(k0 * hd, k1 * hd))]).linear
+        self.o = lin(h, nh * hd, 7, cols=self.q_cols)
+        self.gate_up = tq.MixedLinearGroup([lin(i, h, 9, rows=self.i_cols), lin(i, h, 11, rows=self.i_cols)]).linear
+        self.down = lin(h, i, 13, cols=self.i_cols)
+
+
+def run_prefill_tp(args, ws, rank, device):
+    """Config 2 strong-scaled over the ranks by tensor parallelism: the same block and
+    total work at every N; a step = this rank's four MixedLinear forwards (quantize +
+    mixed GEMM) plus the NCCL all-reduce of the O and down partial outputs."""
+    import torch.distributed as dist
+
+    from tilequant_b200 import _native as N
+
+    full, hidden, acts, rows = _prefill_setup(device)
+    ops = full.linear_ops(rows)
+    shard = BlockShard(rank, ws, device)
+    x_qkv, x_gu = acts["x_qkv"], acts["x_gu"]
+    x_o = acts["x_o"][:, shard.q_cols[0]:shard.q_cols[1]].contiguous()
+    x_down = acts["x_down"][:, shard.i_cols[0]:shard.i_cols[1]].contiguous()
+    del full, acts
+    torch.cuda.empty_cache()
+    flush = torch.empty(int(256e6) // 4, device=device, dtype=torch.float32)
+
+    def step(x_in=None):
+        shard.qkv(x_qkv if x_in is None else x_in)
+        y_o = shard.o(x_o)
+        dist.all_reduce(y_o)
+        shard.gate_up(x_gu)
+        y_d = shard.down(x_down)
+        dist.all_reduce(y_d)
+        return y_d
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        launches0 = N.kernel_launches()
+        evs = [(torch.cuda.Event(True), torch.cuda.Event(True)) for _ in range(args.steps)]
+        with ClockSampler(device.index) as clocks:
+            for e0, e1 in evs:
+                flush.zero_()
+                e0.record()
+                step()
+                e1.record()
+            torch.cuda.synchronize()
+        launches = N.kernel_launches() - launches0
+        _barrier(ws)
+        # the two all-reduces alone, same sizes (50 MB of BF16 each), for the split of the step
+        buf = torch.zeros((rows, LLAMA3B["hidden"]), device=device, dtype=torch.bfloat16)
+        for _ in range(3):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        a0, a1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        a0.record()
+        for _ in range(10):
+            dist.all_reduce(buf)
+            dist.all_reduce(buf)
+        a1.record()
+        torch.cuda.synchronize()
+        # e2e: the step with the hidden states copied in from pinned host memory and the
+        # block's summed down output copied back, every step
+        host_in = hidden.cpu().pin_memory()
+        host_out = torch.empty((rows, LLAMA3B["hidden"]), dtype=torch.bfloat16).pin_memory()
+        _barrier(ws)
+        s0, s1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e2e_steps = max(3, args.steps // 10)
+        s0.record()
+        for _ in range(e2e_steps):
+            y = step(host_in.to(device, non_blocking=True))
+            host_out.copy_(y, non_blocking=True)
+        s1.record()
+        torch.cuda.synchronize()
+        _barrier(ws)
+    ms = _max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps, ws)
+    ar_ms = _max_over_ranks(a0.elapsed_time(a1) / 10, ws)
+    e2e_ms = _max_over_ranks(s0.elapsed_time(s1) / e2e_steps, ws)
+    return {
+        "metric": METRIC_PREFILL, "value": round(ops / (ms * 1e-3) / 1e12, 2), "unit": "TOPS", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 (exact i32 tile products) + bf16, f32 accumulate",
+        "data": "synthetic (seeded random init)",
+        "config": dict(PREFILL_CONFIG, parallelism=f"tp{ws}: Q/K/V and gate/up column-parallel (heads / tiles), "
+                                                  "O and down row-parallel + NCCL all-reduce of BF16 partials"),
+        "tp": {"allreduce_ms_per_step": round(ar_ms, 4), "allreduce_bytes": 2 * rows * LLAMA3B["hidden"] * 2,
+               "gemm_ms_per_step": round(ms - ar_ms, 4),
+               "limiter": "the two 50 MB all-reduces" if ar_ms > 0.5 * ms else "this rank's GEMMs"},
+        "e2e": {"value": round(ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOPS",
+                "h2d_bytes_per_step": hidden.numel() * 2, "d2h_bytes_per_step": hidden.numel() * 2,
+                "what": "the tensor-parallel step with the hidden states copied in from pinned host memory on every "
+                        "rank and the summed block output copied back"},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+    }
 
 
 # ----------------------------------------------------------------- workloads
@@ -847,6 +990,27 @@ def run_reference(args, ws, rank):
     }
 
 
+def _extras(args, device):
+    """The default (prefill) line also carries the decode-side numbers: config 1's
+    decode GEMM (GB/s against HBM) and config 3's greedy generation (tokens/s, TTFT,
+    TPOT), each run with its own short step count."""
+    out = {}
+    sub = argparse.Namespace(**vars(args))
+    sub.steps, sub.warmup = 20, 3
+    d = run_decode(sub, 1, 0, device)
+    out["decode"] = {"what": d["metric"], "value": d["value"], "unit": d["unit"], "us_per_call": d["roofline"]["us_per_call"],
+                     "frac_of_hbm": d["roofline"]["frac"], "hbm_peak_gbs": d["roofline"]["peak"],
+                     "e2e_gbs": d["e2e"]["value"], "cpu_baseline": d.get("cpu_baseline"), "clocks": d["clocks"]}
+    torch.cuda.empty_cache()
+    sub.steps, sub.warmup, sub.model, sub.tp = 3, 2, "llama3b", False
+    gl = run_generate(sub, 1, 0, device)
+    out["generate"] = {"what": gl["metric"], "tokens_per_s": gl["value"], "ttft_ms_p50": gl["ttft_ms_p50"],
+                       "tpot_ms_p50": gl["tpot_ms_p50"], "e2e_tokens_per_s": gl["e2e"]["value"],
+                       "requests_timed": 3, "clocks": gl["clocks"]}
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -862,6 +1026,8 @@ def main():
     ap.add_argument("--keep", type=float, default=KEEP, help="BF16 tile fraction of --workload gemm")
     ap.add_argument("--cpu-rows", type=int, default=256, help="rows per linear in one CPU window")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline leg: seconds of windows")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="prefill: skip the decode (config 1) and generation (config 3) sub-objects")
     args = ap.parse_args()
     ws, rank, local = _dist()
     if args.impl == "reference":
@@ -878,7 +1044,11 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     run = {"decode": run_decode, "gemm": run_gemm, "prefill": run_prefill, "generate": run_generate}[args.workload]
+    if args.workload == "prefill" and ws > 1:
+        run = run_prefill_tp
     line = run(args, ws, rank, device)
+    if args.workload == "prefill" and ws == 1 and not args.no_extras:
+        line.update(_extras(args, device))
     if ws > 1:
         import torch.distributed as dist
 
