@@ -43,9 +43,10 @@ struct RowsArgs {
   int64_t peer_timeout_ns;  // bound of every wait for a peer's partial
 };
 
-// Exchange buffer of the peer sum: 16-byte words [2 (call parity)][world (source rank)]
-// [slots][PEER_WORDS]; word i of a slot holds partial values 2i and 2i+1 (of the 16 rows
-// x 16 columns) interleaved with the call number: {v0, call, v1, call}.
+// Exchange buffer of the peer sum: [2 (call parity)][world (source rank)][slots] slots of
+// 2 KB; a slot holds the 256 partial values (16 rows x 16 columns) of one CTA, one 64-bit
+// word each: {call number (high 32 bits), value bits (low 32 bits)}.  PEER_WORDS counts
+// the slot in 16-byte units.
 constexpr int PEER_WORDS = 128;
 __host__ __device__ constexpr int64_t peer_buffer_bytes(int world, int slots) {
   return (int64_t)2 * world * slots * PEER_WORDS * 16;

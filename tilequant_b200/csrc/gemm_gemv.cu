@@ -30,12 +30,14 @@
 // Row-parallel peer sum (PEER): for a tensor-parallel projection split along K, the
 // partial outputs of the ranks are summed inside this kernel instead of by a separate
 // all-reduce.  CTA b writes its FP32 partial (16 rows x 16 columns) into slot b of every
-// rank's exchange buffer with 16-byte stores over NVLink (the buffers are CUDA IPC
-// mappings), each word carrying two values and, twice, the CTA's call number; so no
-// fence or separate flag is needed: a reader polls each word of its own buffer until
-// both halves hold the current call number (bounded by a timeout that sets an error
-// word, never forever), adds the partials of ranks 0..world-1 in that order, rounds and
-// adds the bias -- the same bits on every rank.  Partials alternate between two halves
+// rank's exchange buffer over NVLink (the buffers are CUDA IPC mappings), one 64-bit
+// word per value: the value's bits and the CTA's call number, stored with one relaxed
+// system-scope 64-bit store.  A 64-bit scalar access is single-copy atomic, so a reader
+// that sees the current call number in a word sees that call's value with it: no fence
+// or separate flag is needed.  A reader polls each word of its own buffer until it holds
+// the current call number (bounded by a timeout that sets an error word, never
+// forever), adds the partials of ranks 0..world-1 in that order, rounds and adds the bias
+// -- the same bits on every rank.  Partials alternate between two halves
 // of the buffer by call parity: a rank can only write call e + 2 after finishing call
 // e + 1, which needed every rank's call e + 1 partial, so every rank has read its call
 // e partials by then.  All CTAs of the grid must be resident at once (the launcher
@@ -71,16 +73,15 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// 16-byte accesses that go to memory every time (peer buffers change under the reader;
-// each aligned 8-byte half is written and read as one unit).
-__device__ __forceinline__ void st_volatile_v4(uint4* p, uint4 v) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
+// Exchange words: {call number (high 32 bits), value bits (low 32 bits)}, written and read
+// with relaxed system-scope 64-bit scalar accesses (single-copy atomic; peer buffers
+// change under the reader, so every read goes to memory).
+__device__ __forceinline__ void st_word(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint4 ld_volatile_v4(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
-               : "memory");
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -235,47 +236,43 @@ __global__ void __launch_bounds__(gv::MAX_S * 32, 2) gemv_kernel(const RowsArgs 
     }
     __syncthreads();
     const uint32_t ep = s_ep;
-    // word i of a slot = {value 2i, call, value 2i+1, call}: a reader that sees the call
-    // number in both halves of a 16-byte word has both values of this call
-    const int64_t par_base = (int64_t)(ep & 1u) * W * slots * PEER_WORDS;
-    for (int i = tid; i < PEER_WORDS * W; i += blockDim.x) {
-      const int p = i / PEER_WORDS, w = i % PEER_WORDS;
-      uint4* dst = reinterpret_cast<uint4*>(a.peer_bufs[p]) + par_base + ((int64_t)a.rank * slots + b) * PEER_WORDS + w;
-      st_volatile_v4(dst, make_uint4(__float_as_uint(red[2 * w]), ep, __float_as_uint(red[2 * w + 1]), ep));
+    // element e of a slot is word e: {call, value bits}
+    constexpr int ELEMS = 2 * PEER_WORDS;  // 256 values per slot, 8 bytes each (the slot's 2 KB)
+    const int64_t par_base = (int64_t)(ep & 1u) * W * slots * ELEMS;
+    for (int i = tid; i < ELEMS * W; i += blockDim.x) {
+      const int p = i / ELEMS, e = i % ELEMS;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(a.peer_bufs[p]) + par_base + ((int64_t)a.rank * slots + b) * ELEMS + e;
+      st_word(dst, ((uint64_t)ep << 32) | __float_as_uint(red[e]));
     }
     // this CTA's slot of every source rank, in this rank's own buffer
-    const uint4* src = reinterpret_cast<const uint4*>(a.peer_bufs[a.rank]) + par_base + (int64_t)b * PEER_WORDS;
-    const int64_t src_stride = (int64_t)slots * PEER_WORDS;
+    const uint64_t* src = reinterpret_cast<const uint64_t*>(a.peer_bufs[a.rank]) + par_base + (int64_t)b * ELEMS;
+    const int64_t src_stride = (int64_t)slots * ELEMS;
     bool gave_up = false;
-    for (int w = tid; w < PEER_WORDS; w += blockDim.x) {
-      float v[2] = {0.0f, 0.0f};
+    for (int e = tid; e < ELEMS; e += blockDim.x) {
+      float v = 0.0f;
       for (int p = 0; p < W; ++p) {  // rank order
-        uint4 q = ld_volatile_v4(src + p * src_stride + w);
-        if ((q.y != ep || q.w != ep) && !gave_up) {
+        uint64_t q = ld_word(src + p * src_stride + e);
+        if ((uint32_t)(q >> 32) != ep && !gave_up) {
           const uint64_t t0 = globaltimer_ns();
-          while (q.y != ep || q.w != ep) {
+          while ((uint32_t)(q >> 32) != ep) {
             if ((int64_t)(globaltimer_ns() - t0) > a.peer_timeout_ns) {
               report(a.err, TQ_ERR_TIMEOUT);
               gave_up = true;
               break;
             }
-            q = ld_volatile_v4(src + p * src_stride + w);
+            q = ld_word(src + p * src_stride + e);
           }
         }
-        const float x0 = __uint_as_float(q.x), x1 = __uint_as_float(q.z);
-        v[0] = p == 0 ? x0 : v[0] + x0;
-        v[1] = p == 0 ? x1 : v[1] + x1;
+        const float x = __uint_as_float((uint32_t)q);
+        v = p == 0 ? x : v + x;
       }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int e = 2 * w + h, j = e >> 4, tok = e & 15;
-        const int cc = r * 64 + 16 * m + j;
-        if (rb + tok < a.n_rows && cc < a.M && a.out) {
-          const int ot = a.out_dtype;
-          uint16_t y = f2h(v[h], ot);
-          if (a.bias) y = f2h(h2f(y, ot) + h2f(reinterpret_cast<const uint16_t*>(a.bias)[cc], ot), ot);
-          reinterpret_cast<uint16_t*>(a.out)[(int64_t)(rb + tok) * a.ldo + cc] = y;
-        }
+      const int j = e >> 4, tok = e & 15;
+      const int cc = r * 64 + 16 * m + j;
+      if (rb + tok < a.n_rows && cc < a.M && a.out) {
+        const int ot = a.out_dtype;
+        uint16_t y = f2h(v, ot);
+        if (a.bias) y = f2h(h2f(y, ot) + h2f(reinterpret_cast<const uint16_t*>(a.bias)[cc], ot), ot);
+        reinterpret_cast<uint16_t*>(a.out)[(int64_t)(rb + tok) * a.ldo + cc] = y;
       }
     }
     return;
