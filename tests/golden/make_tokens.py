@@ -14,12 +14,15 @@ run under ``TRITON_INTERPRET=1`` (with ``make_golden``'s two interpreter work-ar
 its ``tl.range`` patch, and FP32 copies of the 16-bit operands with the FP32 output
 rounded to the 16-bit type afterwards; split 1); the reference's launcher, which needs a CUDA
 stream, is the one thing replaced.  The activation quantizer is the reference's torch
-path.  Greedy decoding runs the Hugging Face model with a dynamic cache: the prompt
+path.  Attention runs on FP32 copies with its output rounded once to FP16 (the numerics of the
+flash attention the reference decodes with; a CPU attention in FP16 is far less
+precise).  Greedy decoding runs the Hugging Face model with a dynamic cache: the prompt
 (batch 8 x 16 seeded ids), then 31 one-token steps, 32 tokens in all -- the tokens the
 reference's CUDA-graph decoder produces for the same model (src/runtime/graph_decode.py
 :428-452 is greedy argmax over the same logits).
 
-Stored per model: the prompt, the 32 tokens, the top-1 minus top-2 logit margin of every
+Stored per model: the prompt, the 32 tokens, the FP16 logits of every step, the top-1
+minus top-2 logit margin of every
 step in FP16 ulps of the top logit (the slack a rounding difference elsewhere in the model
 would have to overcome), the rows whose margin is at least MIN_MARGIN_ULPS at every step,
 the kept tile ids of every projection, and a SHA-256 of the initial weights so the GPU
@@ -79,10 +82,26 @@ def interp_gemm(*, x_fp, x_int8, sx, int8_tiles, int8_scales, int8_tile_ids, int
     return y
 
 
+def _fp32_attention(module, query, key, value, attention_mask, **kwargs):
+    """Hugging Face's SDPA attention on FP32 copies, rounded once to the model's 16-bit
+    type: the numerics of the attention the reference decodes with on the GPU (flash
+    attention accumulates in FP32 and rounds its output once), which a CPU attention
+    computed in FP16 does not reproduce."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    mask = attention_mask.float() if attention_mask is not None and attention_mask.is_floating_point() else attention_mask
+    out, weights = sdpa_attention_forward(module, query.float(), key.float(), value.float(), mask, **kwargs)
+    return out.to(query.dtype), weights
+
+
 def reference_model(name):
+    from transformers import AttentionInterface
+
     spec = MODELS[name]
     model = build(spec)
     sha = state_sha(model)
+    AttentionInterface.register("tilequant_fp32_sdpa", _fp32_attention)
+    model.set_attn_implementation("tilequant_fp32_sdpa")
     cfg = SimpleNamespace(tile_m=64, tile_n=64, pad_to_tile=True, quant_style="gi", dtype_out="fp16")
     keep = {}
     for parent, attr, full, lin in iter_target_linears(model, cfg, model_type=spec["arch"]):
@@ -102,19 +121,20 @@ def reference_model(name):
 @torch.inference_mode()
 def greedy(model, prompt):
     out = model(input_ids=prompt, use_cache=True)
-    tokens, margins = [], []
+    tokens, margins, all_logits = [], [], []
     cache = out.past_key_values
     logits = out.logits[:, -1].float()
     for step in range(NEW_TOKENS):
         tok = logits.argmax(-1)
         tokens.append(tok)
         margins.append(margin_ulps(logits.topk(2, dim=-1).values))
+        all_logits.append(logits.to(DTYPE))
         if step + 1 == NEW_TOKENS:
             break
         out = model(input_ids=tok[:, None], past_key_values=cache, use_cache=True)
         cache = out.past_key_values
         logits = out.logits[:, -1].float()
-    return torch.stack(tokens, 1), torch.stack(margins, 1)
+    return torch.stack(tokens, 1), torch.stack(margins, 1), torch.stack(all_logits, 1)
 
 
 def main():
@@ -125,10 +145,11 @@ def main():
         t0 = time.time()
         model, keep, sha = reference_model(name)
         prompt = torch.randint(0, spec["vocab"], (BATCH, PROMPT_LEN), generator=torch.Generator().manual_seed(spec["seed"] + 5))
-        tokens, margins = greedy(model, prompt)
+        tokens, margins, logits = greedy(model, prompt)
         out[f"{name}__prompt"] = prompt.numpy()
         out[f"{name}__tokens"] = tokens.numpy()
         out[f"{name}__margins"] = margins.numpy()
+        out[f"{name}__logits"] = logits.numpy()
         out[f"{name}__rows"] = np.flatnonzero((margins >= MIN_MARGIN_ULPS).all(1).numpy()).astype(np.int64)
         out[f"{name}__state_sha"] = np.array(sha)
         for full, ids in keep.items():
