@@ -249,6 +249,61 @@ TQ_API int tq_gemm_mixed_peer_sum_noalloc(const int8_t* x_i8, int64_t ld_x8, con
                                           int64_t n_rows, int64_t m, int64_t k, int n_tr, int n_tc, int split_k,
                                           int64_t timeout_ns, int reset_only, int* err, void* stream);
 
+/* ---------------------------------------------------------------- decode step
+ *
+ * The non-GEMM work of one greedy decode step of a Llama/Qwen2 decoder layer, fused.
+ * The reference runs these as torch operators inside its CUDA graph
+ * (src/runtime/graph_decode.py:172-214, the decoder layers of transformers) and its
+ * decode attention as aten._flash_attention_forward with seqused_k
+ * (src/runtime/graph_decode.py:58-70).  16-bit tensors are bf16 or f16 (dtype). */
+
+/* resid_out = resid + delta (16-bit; delta may be NULL: no add, resid_out unused),
+ * y = weight * round16(h * rsqrt(mean(h^2) + eps)) per row: the decoder layer's
+ * residual add and RMSNorm (f32 statistics).  resid_out may alias resid.  hidden is a
+ * multiple of 8 up to 16384; every row starts on a 16-byte boundary. */
+TQ_API int tq_add_rmsnorm(const void* resid, int64_t ld_r, const void* delta, int64_t ld_d, const void* weight,
+                          void* resid_out, int64_t ld_ro, void* y, int64_t ld_y, int64_t n_rows, int64_t hidden,
+                          float eps, int dtype, void* stream);
+
+/* h = round16(round16(silu(gate)) * up) for n_rows <= 128 rows of k columns (gate and
+ * up share the row stride ld_gu), then h's INT8 codes q and per-64-column scales sx
+ * exactly as tq_quantize_act makes them. */
+TQ_API int tq_silu_mul_quant(const void* gate, const void* up, int64_t ld_gu, int64_t n_rows, int64_t k, void* h,
+                             int64_t ld_h, int8_t* q, int64_t ldq, float* sx, int dtype, void* stream);
+
+/* One query token per sequence against a head-major KV cache [B][Hkv][L][D]
+ * (16-byte aligned, contiguous).  q/k/v: the projections' outputs for the token (row
+ * b, head h at + b * ld + h * D).  The kernel applies RoPE (cos/sin: D values of the
+ * current position) to q and k, writes the rotated k and v into cache slot *pos, and
+ * attends over slots [0, *pos] in S splits (ws_*: f32 scratch of B*Hq*S, B*Hq*S,
+ * B*Hq*S*D); *pos is read on the device, so one launch serves every step of a graph. */
+typedef struct tq_attn_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* cos;
+  const void* sin;
+  void* k_cache;
+  void* v_cache;
+  const int64_t* pos;
+  float* ws_m;
+  float* ws_l;
+  float* ws_o;
+  int* err; /* TQ_ERR_TIMEOUT when a TMA load never lands (NULL: not reported) */
+  int64_t ld_q, ld_k, ld_v;
+  int B, Hq, Hkv, D, L, S;
+  float scale_log2; /* softmax scale * log2(e) */
+  int reserved;
+} tq_attn_args;
+
+/* Splits tq_attn_decode should use for this shape on this device (about two CTAs per SM). */
+TQ_API int tq_attn_decode_splits(int batch, int kv_heads, int max_len);
+
+/* out[b, h*D + d] = softmax(q_h k^T * scale) v (16-bit); with q_out, also its INT8 codes
+ * and per-64-column scales sx, as tq_quantize_act would make them from out. */
+TQ_API int tq_attn_decode(const tq_attn_args* args, void* out, int64_t ld_out, int8_t* q_out, int64_t ldq, float* sx,
+                          int dtype, void* stream);
+
 /* ---------------------------------------------------------------- calibration */
 
 /* tile_scores[r, c] += sum over the tile of |f32(W) * f32(G)| (f32 [n_tr][n_tc]).

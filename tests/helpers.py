@@ -75,3 +75,48 @@ def assert_close_gemm(y_bits, ref_bits, what: str = "", rms_frac: float = 1e-3, 
         detail = ", ".join(f"{tuple(i)}: got {y[tuple(i)]:.6g} ref {r[tuple(i)]:.6g}" for i in idx)
         raise AssertionError(f"{what}: {int(bad.sum())} elements beyond tolerance (rms {rms:.4g}): {detail}")
     return np.abs(y - r)
+
+
+def greedy_steps(model, prompt, device, new_tokens: int, eager: bool, forced=None, **prepare_kwargs):
+    """Greedy decoding through CudaGraphGreedyDecoder: the prompt, then new_tokens - 1
+    one-token steps.  With ``forced`` (ids [batch, new_tokens]) each step's input is the
+    forced token instead of the decoder's own pick (teacher forcing), so two arms can be
+    compared over the same history.  ``prepare_kwargs`` go to ``prepare``.  Returns (ids
+    [batch, new_tokens] numpy, logits [batch, new_tokens, vocab] on the CPU)."""
+    import torch
+
+    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
+
+    dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=prompt.shape[1], max_new_tokens=new_tokens,
+                                         batch_size=prompt.shape[0], device=device, eager=eager, **prepare_kwargs)
+    logits = []
+    try:
+        dec.prefill(prompt)
+        logits.append(dec.last_logits.reshape(prompt.shape[0], -1).clone())
+        for step in range(new_tokens - 1):
+            if forced is not None:
+                with torch.inference_mode():
+                    dec._token.copy_(torch.from_numpy(np.ascontiguousarray(forced[:, step:step + 1])).to(device))
+            dec.decode(1)
+            logits.append(dec.last_logits.reshape(prompt.shape[0], -1).clone())
+        ids = dec._generated.clone()
+    finally:
+        dec.close()
+    return ids.cpu().numpy(), torch.stack(logits, 1).cpu()
+
+
+def tracking(ref_ids, ref_logits, our_logits, sure_ulps: float = 32):
+    """How closely teacher-forced logits follow a reference run: the per-step drift
+    max|ours - ref| / max|ref| (over prompts and vocabulary, worst step), the fraction of
+    (prompt, step) whose reference top-1 leads by at least ``sure_ulps`` FP16 ulps, the
+    (prompt, step, lead) of those where the two picks differ, and the fraction of all
+    (prompt, step) where the picks agree."""
+    from tests.golden.tiny_models import margin_ulps
+
+    rl, ol = ref_logits.float(), our_logits.float()
+    drift = (ol - rl).abs().amax(dim=(0, 2)) / rl.abs().amax(dim=(0, 2))
+    margin = margin_ulps(rl.topk(2, dim=-1).values).numpy()
+    sure = margin >= sure_ulps
+    picks = ol.argmax(dim=-1).numpy()
+    bad = [(int(r), int(t), float(margin[r, t])) for r, t in zip(*np.nonzero(sure & (picks != ref_ids)))]
+    return float(drift.max()), float(sure.mean()), bad, float((picks == ref_ids).mean())

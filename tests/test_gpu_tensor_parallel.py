@@ -202,3 +202,85 @@ def test_peer_sum_gemm_two_gpus():
         assert status == 0, rank
         assert same, rank  # the same bits on every rank
         assert not errors, (rank, errors)
+
+
+def _token_worker(rank, world, port, name, peer, out_q):
+    """TP1 (this GPU alone) against TP2 on the greedy-token fixture models: TP1 decodes
+    freely, TP2 is teacher-forced on TP1's tokens."""
+    import datetime
+    import os
+    from pathlib import Path
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from tests.golden import tiny_models as T
+    from tests.helpers import greedy_steps, tracking
+    from tilequant_b200.apply import apply_tile_maps, default_cfg
+    from tilequant_b200.parallel import tensor_parallel_
+    from tilequant_b200.peer import PeerExchange
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    exchange = None
+    try:
+        if peer:
+            exchange = PeerExchange(dev, world, rank).connect()
+        fix = np.load(Path(__file__).resolve().parent / "golden" / "tokens.npz")
+        spec = T.MODELS[name]
+        prefix = f"{name}__keep__"
+        keep = {k[len(prefix):]: torch.from_numpy(fix[k]) for k in fix.files if k.startswith(prefix)}
+        prompt = torch.from_numpy(fix[f"{name}__prompt"])
+        cfg = default_cfg(dtype_out="fp16")
+        one = T.build(spec, dev)
+        apply_tile_maps(one, keep, cfg, model_type=spec["arch"])
+        ref, ref_logits = greedy_steps(one, prompt, dev, T.NEW_TOKENS, eager=False)
+        del one
+        two = T.build(spec, dev)
+        tensor_parallel_(two, rank, world, lambda n, n_tr, n_tc: keep[n], cfg=cfg, model_type=spec["arch"],
+                         exchange=exchange)
+        _, two_logits = greedy_steps(two, prompt, dev, T.NEW_TOKENS, eager=False, forced=ref)
+        same = two_logits.view(torch.int16).to(dev)
+        gathered = [torch.empty_like(same) for _ in range(world)]
+        dist.all_gather(gathered, same)
+        identical = all(torch.equal(g, same) for g in gathered)
+        status = 0 if exchange is None else exchange.status()
+        out_q.put((rank, tracking(ref, ref_logits, two_logits), identical, status))
+    finally:
+        if exchange is not None:
+            torch.cuda.synchronize()
+            dist.barrier()
+            exchange.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,peer", [("llama", False), ("qwen2", False), ("llama", True), ("qwen2", True)])
+def test_tensor_parallel_tokens_follow_tp1(name, peer):
+    """Greedy tokens under TP2 against TP1 over 32 steps (the fixture's FP16 tiny Llama
+    and Qwen2, 10 % 16-bit tiles): the row-parallel sums associate differently from the
+    one-GPU K loop, so TP2 is teacher-forced on TP1's tokens and must keep its logits
+    within 6 % of the logit scale and pick TP1's token wherever TP1's top-1 leads by at
+    least 32 FP16 ulps; both ranks hold bit-identical logits."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_token_worker, args=(r, 2, port, name, peer, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, (drift, sure, bad, agree), identical, status in res:
+        print(f"{name} peer={peer} rank {rank}: drift {drift:.4f}, sure {sure:.2f}, agree {agree:.3f}, "
+              f"differing picks {bad}")
+        assert drift <= 0.06, (rank, drift)
+        assert sure >= 0.6, (rank, sure)
+        assert not bad, (rank, bad)
+        assert identical, rank
+        assert status == 0, rank

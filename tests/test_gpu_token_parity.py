@@ -17,12 +17,12 @@ hands it to the tensor cores), so a last-bit difference there is allowed; our de
 then teacher-forced on the reference arm's tokens and compared step by step where the
 reference's top logit leads by more than the drift such bits leave.
 
-(``tests/golden/tokens.npz`` also holds 32 greedy tokens of the reference's own Python
-model path run on the CPU; ``test_reference_cpu_run_prefix`` compares with it.  There a
-CPU attention and a GPU attention differ in the last FP16 bit of ~16 % of their outputs,
-and every projection re-quantizes its input to INT8, which turns such one-ulp
-differences into ~1 % output differences a layer later, so the agreement is checked only
-as far as the reference's margin exceeds that drift.)
+(``tests/golden/tokens.npz`` also holds 32 greedy tokens and their logits from the
+reference's own Python model path run on the CPU; ``test_reference_cpu_run_teacher_forced``
+follows them.  There a CPU attention and a GPU attention differ in the last FP16 bit of
+~16 % of their outputs, and every projection re-quantizes its input to INT8, which turns
+such one-ulp differences into ~1 % output differences a layer later, so the picks are
+compared where the reference's margin exceeds that drift.)
 """
 
 from __future__ import annotations
@@ -35,6 +35,7 @@ import torch
 
 import tilequant_b200 as tq
 from tests.golden import tiny_models as T
+from tests.helpers import greedy_steps, tracking
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -95,27 +96,7 @@ def _model(name, keep_frac, device, oracle: bool):
 
 
 def _decode(model, prompt, device, eager, forced=None):
-    """Greedy: the prompt, then 31 one-token steps; with ``forced`` (ids [batch, 32]) each
-    step's input is the forced token instead of the decoder's own pick (teacher forcing),
-    so two arms can be compared over the same history."""
-    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
-
-    dec = CudaGraphGreedyDecoder.prepare(model, prompt_tokens=prompt.shape[1], max_new_tokens=T.NEW_TOKENS,
-                                         batch_size=prompt.shape[0], device=device, eager=eager)
-    logits = []
-    try:
-        dec.prefill(prompt)
-        logits.append(dec.last_logits.reshape(prompt.shape[0], -1).clone())
-        for step in range(T.NEW_TOKENS - 1):
-            if forced is not None:
-                with torch.inference_mode():
-                    dec._token.copy_(torch.from_numpy(forced[:, step:step + 1]).to(device))
-            dec.decode(1)
-            logits.append(dec.last_logits.reshape(prompt.shape[0], -1).clone())
-        ids = dec._generated.clone()
-    finally:
-        dec.close()
-    return ids.cpu().numpy(), torch.stack(logits, 1).cpu()
+    return greedy_steps(model, prompt, device, T.NEW_TOKENS, eager, forced)
 
 
 @pytest.mark.parametrize("name", sorted(T.MODELS))
@@ -141,26 +122,28 @@ def test_mixed_tiles_track_reference_arithmetic(cuda_device, name):
     ref, ref_logits = _decode(_model(name, 0.1, cuda_device, oracle=True), prompt, cuda_device, eager=True)
     _, our_logits = _decode(_model(name, 0.1, cuda_device, oracle=False), prompt, cuda_device, eager=False,
                             forced=ref)
-    rl, ol = ref_logits.float(), our_logits.float()
-    drift = (ol - rl).abs().amax(dim=(0, 2)) / rl.abs().amax(dim=(0, 2))
-    assert float(drift.max()) <= 0.04, drift.tolist()
-    margin = T.margin_ulps(rl.topk(2, dim=-1).values).numpy()
-    sure = margin >= 32
-    assert sure.mean() >= 0.6, margin
-    picks = ol.argmax(dim=-1).numpy()
-    bad = [(int(r), int(t), float(margin[r, t])) for r, t in zip(*np.nonzero(sure & (picks != ref)))]
+    drift, sure, bad, agree = tracking(ref, ref_logits, our_logits)
+    assert drift <= 0.04, drift
+    assert sure >= 0.6, sure
     assert not bad, f"(prompt, step, reference lead in ulps) where the tokens differ: {bad}"
 
 
 @pytest.mark.parametrize("name", sorted(T.MODELS))
-def test_reference_cpu_run_prefix(cuda_device, name):
-    """Against the reference's own Python model path (run on the CPU to make the fixture):
-    the first token of every prompt whose reference margin is comfortable (at least 64
-    FP16 ulps), since the prefill logits already carry the CPU/GPU attention drift."""
+def test_reference_cpu_run_teacher_forced(cuda_device, name):
+    """Against the reference's own Python model path (run on the CPU to make the
+    fixture), our decoder teacher-forced on the reference's 32 tokens: the logits stay
+    within 6 % of the logit scale of the reference's (measured <= 5 %: the CPU/GPU
+    attention and norm drift on top of the 16-bit tile bits), the picks agree at 95 % of
+    the steps or more, and everywhere the reference's top-1 leads by at least 64 FP16
+    ulps (about two thirds of the steps of these fixtures; the largest lead at which the
+    picks were seen to differ was 52 ulps)."""
     prompt = torch.from_numpy(FIX[f"{name}__prompt"])
-    ours, _ = _decode(_model(name, 0.1, cuda_device, oracle=False), prompt, cuda_device, eager=False)
-    ref = FIX[f"{name}__tokens"]
-    first_margin = FIX[f"{name}__margins"][:, 0]
-    sure = first_margin >= 64
-    assert sure.sum() >= 2
-    np.testing.assert_array_equal(ours[sure, 0], ref[sure, 0])
+    ref, ref_logits = FIX[f"{name}__tokens"], torch.from_numpy(FIX[f"{name}__logits"])
+    _, our_logits = _decode(_model(name, 0.1, cuda_device, oracle=False), prompt, cuda_device, eager=False,
+                            forced=ref)
+    drift, sure, bad, agree = tracking(ref, ref_logits, our_logits, sure_ulps=64)
+    print(f"{name}: drift {drift:.4f}, sure {sure:.2f}, agree {agree:.3f}")
+    assert drift <= 0.06, drift
+    assert sure >= 0.5, sure
+    assert agree >= 0.95, agree
+    assert not bad, f"(prompt, step, reference lead in ulps) where the tokens differ: {bad}"

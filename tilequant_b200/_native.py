@@ -20,7 +20,17 @@ TQ_DTYPE_BF16, TQ_DTYPE_F16 = 0, 1
 TQ_ALGO_AUTO, TQ_ALGO_ROWS, TQ_ALGO_UMMA, TQ_ALGO_GEMV = 0, 1, 2, 3
 ABI_VERSION = 1
 
-_P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+_P, _I64, _I, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
+
+
+class AttnArgs(ctypes.Structure):
+    """``tq_attn_args`` of the header, field for field."""
+
+    _fields_ = [(name, _P) for name in ("q", "k", "v", "cos", "sin", "k_cache", "v_cache", "pos", "ws_m", "ws_l",
+                                        "ws_o", "err")] + \
+               [(name, _I64) for name in ("ld_q", "ld_k", "ld_v")] + \
+               [(name, _I) for name in ("B", "Hq", "Hkv", "D", "L", "S")] + \
+               [("scale_log2", ctypes.c_float), ("reserved", _I)]
 
 # name -> argument types, in header order
 SIGNATURES = {
@@ -39,6 +49,10 @@ SIGNATURES = {
     "tq_gemm_int8_partials": [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _I, _P],
     "tq_pack_int8_tiles": [_P, _I, _I64, _I64, _I64, _I, _P, _I64, _P, _P, _P, _P],
     "tq_gather_fp_tiles": [_P, _I, _I64, _I64, _I64, _I, _P, _I64, _P, _P],
+    "tq_add_rmsnorm": [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _I64, _I64, _F, _I, _P],
+    "tq_silu_mul_quant": [_P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P],
+    "tq_attn_decode_splits": [_I, _I, _I],
+    "tq_attn_decode": [ctypes.POINTER(AttnArgs), _P, _I64, _P, _I64, _P, _I, _P],
     "tq_calib_gi_accumulate": [_P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _P],
     "tq_calib_iaa_channel_accumulate": [_P, _I, _I64, _I64, _I64, _P, _P],
     "tq_calib_iaa_tile_scores": [_P, _I, _I64, _I64, _I64, _P, _I64, _P, _P, _P],

@@ -57,6 +57,31 @@ __device__ __forceinline__ int quant_code_fast(float v, float s, float r) {
   return (int)k;
 }
 
+// Maximum over the CTA (every thread gets it); `red` holds 32 floats of shared memory.
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+// Activation tile scale from its absmax: the quotient rounded to the 16-bit type, 1 for
+// an all-zero tile (quant_utils.py:41-74).
+template <int XT>
+__device__ __forceinline__ float scale_from_absmax(float amax) {
+  return amax > 0.0f ? round16(__fdiv_rn(amax, 127.0f), XT) : 1.0f;
+}
+
 __device__ __forceinline__ void report(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }

@@ -42,28 +42,6 @@ __device__ __forceinline__ float absmax8(uint4 v) {
   return m;
 }
 
-__device__ __forceinline__ float block_max(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    v = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (lane == 0) red[0] = v;
-  }
-  __syncthreads();
-  return red[0];
-}
-
-template <int XT>
-__device__ __forceinline__ float scale_from_absmax(float amax) {
-  return amax > 0.0f ? round16(__fdiv_rn(amax, 127.0f), XT) : 1.0f;
-}
-
 // Absmax of column tile blockIdx.x over rows [row0, row1).  vec: 16-byte path allowed.
 template <int XT>
 __device__ float tile_absmax(const void* x, int64_t n_rows, int64_t k, int64_t ld_row, int64_t ld_col,

@@ -13,13 +13,19 @@ How the graphs are built here:
   cache is a transformers ``StaticCache`` whose storage never moves, and the decode
   graph keeps the current token and position on the GPU, so replays need no host
   input at all;
-* attention is a registered transformers attention function: prefill runs causal
-  SDPA over the prompt prefix of the cache; decode runs SDPA of the single query over
-  the whole static cache with an additive mask, built on the GPU inside the graph from
-  the position tensor, that hides the slots past the current position;
-* the projections run the mixed tile GEMM kernels of this package (decode: quantizer
-  + register-fragment decode kernel; prefill: quantizer + tcgen05 kernel), so one
-  replay launches exactly the kernels of one eager forward.
+* prefill runs the transformers forward with a registered attention function (causal
+  SDPA over the prompt prefix of the cache) and the mixed tile GEMM kernels of this
+  package (quantizer + tcgen05 kernel) for the projections;
+* decode runs ``FusedDecodeStep`` (decode_step.py) for Llama/Qwen2 decoders: per layer
+  a fused residual-add + RMSNorm, the QKV GEMM, one decode-attention kernel pair (RoPE,
+  cache write, split-KV attention over the valid prefix only, the O projection's input
+  quantization), the O GEMM, the second norm, the gate/up GEMM, SiLU * up with the down
+  projection's input quantization and the down GEMM -- the reference's flash-attention
+  decode (src/runtime/graph_decode.py:58-70) reads the valid prefix the same way.
+  Other models (or ``fused_decode=False``) decode through the transformers forward with
+  SDPA of the single query over the whole static cache and an additive mask built on
+  the GPU from the position tensor;
+* one replay launches exactly the kernels of one eager body.
 """
 
 from __future__ import annotations
@@ -87,7 +93,8 @@ class CudaGraphGreedyDecoder:
     """
 
     def __init__(self, model: torch.nn.Module, *, prompt_tokens: int, max_new_tokens: int, batch_size: int = 1,
-                 device: Union[torch.device, str] = "cuda", prefill_only: bool = False, eager: bool = False) -> None:
+                 device: Union[torch.device, str] = "cuda", prefill_only: bool = False, eager: bool = False,
+                 fused_decode: bool = True) -> None:
         from transformers import StaticCache
 
         if prompt_tokens < 1:
@@ -118,6 +125,8 @@ class CudaGraphGreedyDecoder:
         self.max_cache_len = self.prompt_tokens + (0 if prefill_only else self.max_new_tokens)
         self._prefill_only = prefill_only
         self._eager = eager
+        self._fused_decode = fused_decode
+        self._step = None  # FusedDecodeStep, built once the prefill has allocated the cache
         self.cache = StaticCache(config=model.config, max_cache_len=self.max_cache_len)
         self._in_prefill = True
         dev = self.device
@@ -177,6 +186,7 @@ class CudaGraphGreedyDecoder:
                 delattr(m, _DECODER_ATTRIBUTE)
         self.model.set_attn_implementation(attn_implementation or self._previous_attention)
         self._prefill_graph = self._decode_graph = None
+        self._step = None
         self.cache = None
         self._prefill_logits = self._decode_logits = self.last_logits = None
 
@@ -185,11 +195,11 @@ class CudaGraphGreedyDecoder:
     @torch.inference_mode()
     def prepare(cls, model: torch.nn.Module, *, prompt_tokens: int = 128, max_new_tokens: int = 512,
                 batch_size: int = 1, device: Union[torch.device, str] = "cuda", prefill_only: bool = False,
-                eager: bool = False) -> "CudaGraphGreedyDecoder":
+                eager: bool = False, fused_decode: bool = True) -> "CudaGraphGreedyDecoder":
         """Allocate, warm up and capture the prefill and decode graphs (outside any
         request timing)."""
         dec = cls(model, prompt_tokens=prompt_tokens, max_new_tokens=max_new_tokens, batch_size=batch_size,
-                  device=device, prefill_only=prefill_only, eager=eager)
+                  device=device, prefill_only=prefill_only, eager=eager, fused_decode=fused_decode)
         try:
             dec._capture()
         except BaseException:
@@ -202,6 +212,11 @@ class CudaGraphGreedyDecoder:
         decode = not self._prefill_only and self.max_new_tokens > 1
         # eager warm-up: the cache's storage and every kernel's lazy state exist before capture
         self._prefill_body()
+        if decode and self._fused_decode:
+            from .decode_step import FusedDecodeStep
+
+            if FusedDecodeStep.unsupported_reason(self.model) is None:
+                self._step = FusedDecodeStep(self.model, self.cache, self.batch_size, self.device)
         if decode:
             self._decode_body()
         torch.cuda.synchronize(self.device)
@@ -249,14 +264,17 @@ class CudaGraphGreedyDecoder:
     @torch.inference_mode()
     def _decode_body(self) -> None:
         self._in_prefill = False
-        # additive mask over the static cache: slots past the current position are hidden
-        self._decode_mask.copy_(torch.where(self._slots <= self._position, 0.0, float("-inf"))
-                                .to(self._decode_mask.dtype).view(1, 1, 1, -1))
-        out = self.model(input_ids=self._token, attention_mask=None, position_ids=self._position.view(1, 1),
-                         past_key_values=self.cache, cache_position=self._position, use_cache=True,
-                         logits_to_keep=1)
-        self._decode_logits = out.logits
-        self._next.copy_(out.logits[:, -1:].argmax(dim=-1))
+        if self._step is not None:
+            self._decode_logits = self._step(self._token, self._position)
+        else:
+            # additive mask over the static cache: slots past the current position are hidden
+            self._decode_mask.copy_(torch.where(self._slots <= self._position, 0.0, float("-inf"))
+                                    .to(self._decode_mask.dtype).view(1, 1, 1, -1))
+            out = self.model(input_ids=self._token, attention_mask=None, position_ids=self._position.view(1, 1),
+                             past_key_values=self.cache, cache_position=self._position, use_cache=True,
+                             logits_to_keep=1)
+            self._decode_logits = out.logits
+        self._next.copy_(self._decode_logits[:, -1:].argmax(dim=-1))
         # position P consumes generated token P - prompt and produces token P - prompt + 1
         idx = (self._position - self.prompt_tokens + 1).view(1, 1).expand(self.batch_size, 1)
         self._generated.scatter_(1, idx, self._next)
