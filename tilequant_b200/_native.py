@@ -17,7 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libtilequant_b200.so"
 
 TQ_OK, TQ_ERR_INVALID, TQ_ERR_UNSUPPORTED, TQ_ERR_CUDA, TQ_ERR_TIMEOUT = range(5)
 TQ_DTYPE_BF16, TQ_DTYPE_F16 = 0, 1
-TQ_ALGO_AUTO, TQ_ALGO_ROWS, TQ_ALGO_UMMA, TQ_ALGO_GEMV = 0, 1, 2, 3
+TQ_ALGO_AUTO, TQ_ALGO_ROWS, TQ_ALGO_UMMA, TQ_ALGO_GEMV, TQ_ALGO_STREAM = 0, 1, 2, 3, 4
 ABI_VERSION = 1
 
 _P, _I64, _I, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float

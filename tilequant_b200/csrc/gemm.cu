@@ -12,6 +12,9 @@ int tq_gemv_supported(const tq::RowsArgs& a);
 int tq_gemv_peer_supported(const tq::RowsArgs& a);
 int tq_gemv_preferred(const tq::RowsArgs& a, int n_tr);
 int tq_launch_gemv(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
+int tq_stream_split(int n_tr, int n_tc, int n_rows);
+int tq_stream_supported(const tq::RowsArgs& a);
+int tq_launch_stream(tq::RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st);
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
@@ -96,9 +99,17 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
       return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: unsupported shape or alignment");
     return tq_launch_umma(a, n_tr, fp_dtype, st);
   }
-  if (algo == TQ_ALGO_GEMV || (algo == TQ_ALGO_AUTO && tq_gemv_preferred(a, n_tr))) {
+  if (algo == TQ_ALGO_STREAM || (algo == TQ_ALGO_AUTO && n_rows <= 16)) {
+    // decode: the stream kernel at its split; where it cannot take the call (alignment,
+    // shared memory), the row kernel at the same split gives the same bits
+    if (a.split == 0) a.split = tq_stream_split(n_tr, n_tc, (int)n_rows);
+    if (tq_stream_supported(a)) return tq_launch_stream(a, n_tr, fp_dtype, st);
+    if (algo == TQ_ALGO_STREAM) return tq_set_error(TQ_ERR_UNSUPPORTED, "stream decode kernel: unsupported call");
+    return tq_launch_rows(a, n_tr, fp_dtype, st, t16);
+  }
+  if (algo == TQ_ALGO_GEMV) {
     // asked for by name, the decode kernel also runs 17..64 rows as 16-row blocks
-    if (!(algo == TQ_ALGO_GEMV ? tq_gemv_peer_supported(a) : tq_gemv_supported(a)))
+    if (!tq_gemv_peer_supported(a))
       return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: needs <= 64 rows and split_k <= 8");
     return tq_launch_gemv(a, n_tr, fp_dtype, st);
   }

@@ -27,6 +27,7 @@ struct RowsArgs {
   int n_rows, M, K, n_tc, split;
   int n_tr;            // row tiles of the weight
   int rows_per_cta;    // row tiles one CTA streams (rows kernel, split 1)
+  int ring_chunks;     // 16 KB chunks in the weight ring (stream kernel)
   int64_t w8_rows;     // 64 * T8 (rows of the INT8 arena)
   int64_t w16_rows;    // 64 * T16
   int has_fp16;
