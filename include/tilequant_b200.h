@@ -302,13 +302,24 @@ typedef struct tq_attn_args {
   int reserved;
 } tq_attn_args;
 
-/* Splits tq_attn_decode should use for this shape on this device (about two CTAs per SM). */
+/* Splits tq_attn_decode should use for this shape on this device: as many as keep every
+ * CTA resident at once (two per SM). */
 TQ_API int tq_attn_decode_splits(int batch, int kv_heads, int max_len);
 
 /* out[b, h*D + d] = softmax(q_h k^T * scale) v (16-bit); with q_out, also its INT8 codes
  * and per-64-column scales sx, as tq_quantize_act would make them from out. */
 TQ_API int tq_attn_decode(const tq_attn_args* args, void* out, int64_t ld_out, int8_t* q_out, int64_t ldq, float* sx,
                           int dtype, void* stream);
+
+/* Greedy pick of a decode step: next[b] = token[b] = argmax of logits row b (the first
+ * index of the maximum, as torch.argmax), generated[b, *position - prompt_tokens + 1] =
+ * that id (skipped outside 0..gen_cols-1), then *position += 1 -- the bookkeeping of the
+ * reference's decode body (src/runtime/graph_decode.py:428-452).  keys: n_rows uint64 of
+ * scratch, zero before the first call; each call leaves them zero.  next, token and
+ * generated may be NULL. */
+TQ_API int tq_greedy_pick(const void* logits, int64_t ld, int64_t n_rows, int64_t vocab, int dtype,
+                          unsigned long long* keys, int64_t* next, int64_t* token, int64_t* generated,
+                          int64_t gen_ld, int64_t gen_cols, int64_t* position, int64_t prompt_tokens, void* stream);
 
 /* ---------------------------------------------------------------- calibration */
 

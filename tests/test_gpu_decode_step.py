@@ -196,3 +196,33 @@ def test_fused_step_tracks_transformers_forward(cuda_device, arch):
     assert drift <= 0.06, drift
     assert sure >= 0.6, sure
     assert not bad, bad
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("B,V", [(1, 512), (4, 128256), (16, 152064), (3, 5000)])
+def test_greedy_pick_matches_torch_argmax_and_bookkeeping(cuda_device, dtype, B, V):
+    """argmax (first index of the maximum, ties included), the next token, the generated
+    id at position - prompt + 1 and the advanced position, over three calls in a row
+    (the scratch keys are left zero by each)."""
+    from tilequant_b200.decode_step import greedy_pick
+
+    g = torch.Generator(device=cuda_device).manual_seed(B + V)
+    prompt, T = 10, 5
+    keys = torch.zeros(B, dtype=torch.long, device=cuda_device)
+    position = torch.tensor([prompt], dtype=torch.long, device=cuda_device)
+    nxt = torch.zeros(B, 1, dtype=torch.long, device=cuda_device)
+    tok = torch.zeros(B, 1, dtype=torch.long, device=cuda_device)
+    gen = torch.full((B, T), -1, dtype=torch.long, device=cuda_device)
+    for call in range(3):
+        logits = (torch.randn(B, V, device=cuda_device, generator=g) * 4).to(dtype)
+        logits[0, V // 3] = logits[0, V // 2] = logits[0].max() + 1  # a tie: the first index wins
+        if B > 1:
+            logits[1] = -logits[1].abs()  # an all-negative row
+        want = logits.argmax(dim=-1)
+        greedy_pick(logits, keys, position, prompt, nxt, tok, gen)
+        torch.cuda.synchronize()
+        assert torch.equal(nxt.view(-1), want) and torch.equal(tok.view(-1), want), call
+        assert int(want[0]) == V // 3
+        assert torch.equal(gen[:, call + 1], want), call
+        assert int(position.item()) == prompt + call + 1
+        assert int(keys.abs().sum().item()) == 0

@@ -53,6 +53,7 @@ SIGNATURES = {
     "tq_silu_mul_quant": [_P, _P, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _I, _P],
     "tq_attn_decode_splits": [_I, _I, _I],
     "tq_attn_decode": [ctypes.POINTER(AttnArgs), _P, _I64, _P, _I64, _P, _I, _P],
+    "tq_greedy_pick": [_P, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _I64, _P, _I64, _P],
     "tq_calib_gi_accumulate": [_P, _P, _I, _I64, _I64, _I64, _I64, _I, _I, _P, _P],
     "tq_calib_iaa_channel_accumulate": [_P, _I, _I64, _I64, _I64, _P, _P],
     "tq_calib_iaa_tile_scores": [_P, _I, _I64, _I64, _I64, _P, _I64, _P, _P, _P],

@@ -11,8 +11,8 @@
 //                           into the cache, then a split of the valid cache prefix
 //                           streamed through shared memory by TMA and reduced on the
 //                           tensor cores with an online softmax
-//   attn_combine_kernel     the splits of one query head merged, the output rounded to
-//                           16 bits and quantized per 64-column tile for the O projection
+//   attn_combine_kernel     the splits of one 64-column tile of a query head merged, the
+//                           output rounded to 16 bits and quantized for the O projection
 //   silu_mul_quant_kernel   a = silu(gate), h = a * up (16-bit), quantized per tile
 //
 // Elementwise arithmetic follows the decoder's own torch code operation by operation
@@ -405,22 +405,23 @@ __global__ void __launch_bounds__(at::WARPS * 32) attn_partial_kernel(const Attn
   }
 }
 
-// One CTA per query head, every batch row: merge the splits (a warp per row computes
-// the row's max and the split weights; then each thread sums the weighted partials of
-// its outputs, the split loads in flight together), round to 16 bits, then the INT8
-// codes and scale of each 64-column tile of the head (all rows share a scale).
+// One CTA per 64-column tile of a query head (D / 64 per head), every batch row: merge
+// the splits (a warp per row computes the row's max and the split weights; then each
+// thread sums the weighted partials of one output, the split loads in flight together),
+// round to 16 bits, then the tile's INT8 codes and scale (all rows share a scale).
 template <int XT, int D>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a, void* __restrict__ out, int64_t ld_out,
                                                            int8_t* __restrict__ q, int64_t ldq,
                                                            float* __restrict__ sx) {
   extern __shared__ float sm[];
-  float* vals = sm;                   // B x D outputs
-  float* wts = sm + a.B * D;          // B x S split weights
+  float* vals = sm;                   // B x 64 outputs of this tile
+  float* wts = sm + a.B * 64;         // B x S split weights
   float* inv_l = wts + a.B * a.S;     // B: 1 / total sum (0 for an empty row)
   __shared__ float red[32];
   grid_dep_wait();
   grid_dep_launch();
-  const int h = blockIdx.x, S = a.S, B = a.B;
+  constexpr int TPH = D / 64;  // column tiles per head
+  const int h = blockIdx.x / TPH, tile = blockIdx.x % TPH, S = a.S, B = a.B;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int b = warp; b < B; b += nw) {
     const int64_t base = ((int64_t)b * a.Hq + h) * S;
@@ -438,8 +439,9 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a, voi
     if (lane == 0) inv_l[b] = ls > 0.0f ? 1.0f / ls : 0.0f;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < B * D; e += blockDim.x) {
-    const int b = e / D, d = e % D;
+  float mv = 0.0f;
+  for (int e = threadIdx.x; e < B * 64; e += blockDim.x) {
+    const int b = e >> 6, d = tile * 64 + (e & 63);
     const float* po = a.ws_o + (((int64_t)b * a.Hq + h) * S) * D + d;
     const float* wb = wts + b * S;
     float acc = 0.0f;
@@ -447,23 +449,75 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const AttnArgs a, voi
     for (int s = 0; s < S; ++s) acc = fmaf(po[(int64_t)s * D], wb[s], acc);
     const float v = round16(acc * inv_l[b], XT);
     vals[e] = v;
+    mv = fmaxf(mv, fabsf(v));
     sth<XT>(out, (int64_t)b * ld_out + (int64_t)h * D + d, v);
   }
   if (!q) return;
-  __syncthreads();
-#pragma unroll
-  for (int t = 0; t < D / 64; ++t) {
-    float mv = 0.0f;
-    for (int e = threadIdx.x; e < B * 64; e += blockDim.x) mv = fmaxf(mv, fabsf(vals[(e >> 6) * D + t * 64 + (e & 63)]));
-    mv = block_max(mv, red);
-    const float sc = scale_from_absmax<XT>(mv);
-    const float rc = __frcp_rn(sc);
-    for (int e = threadIdx.x; e < B * 64; e += blockDim.x) {
-      const int b = e >> 6, j = e & 63;
-      q[(int64_t)b * ldq + (int64_t)h * D + t * 64 + j] = (int8_t)quant_code_fast(vals[b * D + t * 64 + j], sc, rc);
-    }
-    if (threadIdx.x == 0) sx[h * (D / 64) + t] = sc;
+  mv = block_max(mv, red);  // also orders the vals writes before the reads below
+  const float sc = scale_from_absmax<XT>(mv);
+  const float rc = __frcp_rn(sc);
+  for (int e = threadIdx.x; e < B * 64; e += blockDim.x) {
+    const int b = e >> 6, j = e & 63;
+    q[(int64_t)b * ldq + (int64_t)h * D + tile * 64 + j] = (int8_t)quant_code_fast(vals[e], sc, rc);
   }
+  if (threadIdx.x == 0) sx[h * TPH + tile] = sc;
+}
+
+// ------------------------------------------------------------------ greedy pick
+// argmax over each row of the logits (the first index of the maximum, as torch.argmax),
+// then the decoder's bookkeeping: the token becomes the next input, is stored in the
+// generated ids at column (position - prompt + 1), and the position advances.
+// Pass 1 (grid: chunks x rows): each CTA's (max, first index) of its chunk, folded into
+// a per-row 64-bit key with atomicMax: high word the value's bits made order-preserving,
+// low word ~index, so the larger value wins and, among equal values, the smaller index.
+__device__ __forceinline__ uint64_t pick_key(float v, uint32_t idx) {
+  const uint32_t u = __float_as_uint(v);
+  const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((uint64_t)ord << 32) | (uint64_t)(0xFFFFFFFFu - idx);
+}
+
+template <int XT>
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const void* __restrict__ logits, int64_t ld, int V,
+                                                             int chunk, unsigned long long* __restrict__ keys) {
+  __shared__ unsigned long long red[8];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int row = blockIdx.y;
+  const int lo = blockIdx.x * chunk, hi = min(V, lo + chunk);
+  uint64_t best = 0;
+  for (int j = lo + threadIdx.x; j < hi; j += blockDim.x) {
+    const uint64_t k = pick_key(ldh<XT>(logits, (int64_t)row * ld + j), (uint32_t)j);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    atomicMax(keys + row, (unsigned long long)best);
+  }
+}
+
+// Pass 2 (one CTA): decode the keys, write the bookkeeping, clear the keys for the next call.
+__global__ void argmax_finish_kernel(unsigned long long* __restrict__ keys, int B, int64_t* __restrict__ next,
+                                     int64_t* __restrict__ token, int64_t* __restrict__ generated, int64_t gen_ld,
+                                     int64_t gen_cols, int64_t* __restrict__ position, int64_t prompt_tokens) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t col = *position - prompt_tokens + 1;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int64_t id = (int64_t)(0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull));
+    keys[b] = 0ull;
+    if (next) next[b] = id;
+    if (token) token[b] = id;
+    if (generated && col >= 0 && col < gen_cols) generated[(int64_t)b * gen_ld + col] = id;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && position) *position += 1;
 }
 
 }  // namespace tq
@@ -529,7 +583,9 @@ extern "C" int tq_silu_mul_quant(const void* gate, const void* up, int64_t ld_gu
 
 extern "C" int tq_attn_decode_splits(int batch, int kv_heads, int max_len) {
   if (batch <= 0 || kv_heads <= 0 || max_len <= 0) return 1;
-  const int want = (2 * tq_sm_count() + batch * kv_heads - 1) / (batch * kv_heads);  // about two CTAs per SM
+  // as many splits as keep every CTA resident at once (two per SM at this kernel's
+  // shared memory), so no split waits for a second wave
+  const int want = (2 * tq_sm_count()) / (batch * kv_heads);
   const int chunks = (max_len + at::CH - 1) / at::CH;
   return std::max(1, std::min({want, chunks, 64}));
 }
@@ -551,9 +607,9 @@ static int launch_attn(const AttnArgs& a, const AttnMaps& maps, void* out, int64
   cfg.numAttrs = tq_pdl_enabled() ? 1 : 0;
   TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_partial_kernel<XT, D>, a, maps));
   tq_count_launch();
-  cfg.gridDim = dim3((unsigned)a.Hq, 1, 1);
+  cfg.gridDim = dim3((unsigned)(a.Hq * (D / 64)), 1, 1);
   cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = ((size_t)a.B * D + (size_t)a.B * a.S + a.B) * 4;
+  cfg.dynamicSmemBytes = ((size_t)a.B * 64 + (size_t)a.B * a.S + a.B) * 4;
   TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_combine_kernel<XT, D>, a, out, ld_out, q_out, ldq, sx));
   tq_count_launch();
   return TQ_OK;
@@ -591,4 +647,37 @@ extern "C" int tq_attn_decode(const AttnArgs* args, void* out, int64_t ld_out, i
                       : launch_attn<TQ_DTYPE_BF16, 64>(a, maps, out, ld_out, q_out, ldq, sx, st);
   return a.D == 128 ? launch_attn<TQ_DTYPE_F16, 128>(a, maps, out, ld_out, q_out, ldq, sx, st)
                     : launch_attn<TQ_DTYPE_F16, 64>(a, maps, out, ld_out, q_out, ldq, sx, st);
+}
+
+extern "C" int tq_greedy_pick(const void* logits, int64_t ld, int64_t n_rows, int64_t vocab, int dtype,
+                              unsigned long long* keys, int64_t* next, int64_t* token, int64_t* generated,
+                              int64_t gen_ld, int64_t gen_cols, int64_t* position, int64_t prompt_tokens,
+                              void* stream) {
+  if (dtype != TQ_DTYPE_BF16 && dtype != TQ_DTYPE_F16) return tq_set_error(TQ_ERR_INVALID, "dtype must be bf16 or f16");
+  if (n_rows <= 0 || n_rows > 1024 || vocab <= 0 || vocab > INT32_MAX / 2 || ld < vocab)
+    return tq_set_error(TQ_ERR_INVALID, "greedy pick: 1..1024 rows of vocab <= ld logits");
+  if (!logits || !keys || !position) return tq_set_error(TQ_ERR_INVALID, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int chunk = 4096;
+  const dim3 grid((unsigned)((vocab + chunk - 1) / chunk), (unsigned)n_rows, 1);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = tq_pdl_enabled() ? 1 : 0;
+  if (dtype == TQ_DTYPE_BF16)
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, argmax_partial_kernel<TQ_DTYPE_BF16>, logits, ld, (int)vocab, chunk, keys));
+  else
+    TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, argmax_partial_kernel<TQ_DTYPE_F16>, logits, ld, (int)vocab, chunk, keys));
+  tq_count_launch();
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, argmax_finish_kernel, keys, (int)n_rows, next, token, generated, gen_ld, gen_cols,
+                                 position, prompt_tokens));
+  tq_count_launch();
+  return TQ_OK;
 }

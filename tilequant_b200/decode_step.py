@@ -133,6 +133,31 @@ def attn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Te
     return out
 
 
+def greedy_pick(logits: torch.Tensor, keys: torch.Tensor, position: torch.Tensor, prompt_tokens: int,
+                next_ids: Optional[torch.Tensor] = None, token: Optional[torch.Tensor] = None,
+                generated: Optional[torch.Tensor] = None) -> None:
+    """The greedy decode step's pick and bookkeeping in two kernels: argmax of every row
+    of ``logits`` [B, V] (first index of the maximum, as ``torch.argmax``) into
+    ``next_ids`` and ``token`` ([B, 1] int64), into ``generated[:, position - prompt + 1]``,
+    then ``position += 1``.  ``keys``: [B] int64 scratch, zero before the first call and
+    left zero by every call."""
+    N.require_cuda(logits, keys, position, next_ids, token, generated)
+    B, V = logits.shape
+    if logits.stride(1) != 1 or keys.dtype != torch.int64 or keys.numel() < B or position.dtype != torch.int64:
+        raise ValueError("greedy_pick: unit-stride logits, int64 keys and position")
+    for t in (next_ids, token):
+        if t is not None and (t.dtype != torch.int64 or t.numel() != B or not t.is_contiguous()):
+            raise ValueError("greedy_pick: next/token must be contiguous int64 [B] tensors")
+    if generated is not None and (generated.dtype != torch.int64 or generated.shape[0] != B or generated.stride(1) != 1):
+        raise ValueError("greedy_pick: generated must be int64 [B, T] with unit column stride")
+    lib = N.load()
+    N.check(lib.tq_greedy_pick(logits.data_ptr(), logits.stride(0), B, V, N.dtype_code(logits.dtype), keys.data_ptr(),
+                               N.ptr(next_ids), N.ptr(token), N.ptr(generated),
+                               0 if generated is None else generated.stride(0),
+                               0 if generated is None else generated.shape[1], position.data_ptr(), int(prompt_tokens),
+                               N.stream_of(logits)), "greedy_pick")
+
+
 def _proj(mod: nn.Module, x: torch.Tensor, q: Optional[torch.Tensor] = None,
           sx: Optional[torch.Tensor] = None) -> torch.Tensor:
     """A projection of 2-D activations; a plain MixedLinear takes the given codes."""

@@ -127,6 +127,7 @@ class CudaGraphGreedyDecoder:
         self._eager = eager
         self._fused_decode = fused_decode
         self._step = None  # FusedDecodeStep, built once the prefill has allocated the cache
+        self._pick_keys = None  # greedy_pick scratch of the fused step
         self.cache = StaticCache(config=model.config, max_cache_len=self.max_cache_len)
         self._in_prefill = True
         dev = self.device
@@ -217,6 +218,7 @@ class CudaGraphGreedyDecoder:
 
             if FusedDecodeStep.unsupported_reason(self.model) is None:
                 self._step = FusedDecodeStep(self.model, self.cache, self.batch_size, self.device)
+                self._pick_keys = torch.zeros(self.batch_size, dtype=torch.long, device=self.device)
         if decode:
             self._decode_body()
         torch.cuda.synchronize(self.device)
@@ -265,7 +267,13 @@ class CudaGraphGreedyDecoder:
     def _decode_body(self) -> None:
         self._in_prefill = False
         if self._step is not None:
+            from .decode_step import greedy_pick
+
             self._decode_logits = self._step(self._token, self._position)
+            # argmax + next token + generated ids + position, in two kernels
+            greedy_pick(self._decode_logits.view(self.batch_size, -1), self._pick_keys, self._position,
+                        self.prompt_tokens, self._next, self._token, self._generated)
+            return
         else:
             # additive mask over the static cache: slots past the current position are hidden
             self._decode_mask.copy_(torch.where(self._slots <= self._position, 0.0, float("-inf"))
