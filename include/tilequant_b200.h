@@ -129,7 +129,8 @@ TQ_API int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, con
                   int n_tr, int n_tc, int split_k, int algo, int* err, void* stream);
 
 /* Decode form with the activation quantizer fused into the GEMM prologue: the same
- * result as tq_quantize_act followed by tq_gemm_mixed, in one launch.  n_rows <= 64.
+ * result as tq_quantize_act followed by tq_gemm_mixed, in one launch.  n_rows <= 64; up
+ * to 16 rows it runs the stream kernel, whose splits each quantize their own columns.
  * replaces quantize_activation_tile_absmax + gemm_mixed_rows_splitk as called by
  * MixedLinear.forward for small row counts (src/models/mixed_linear.py:232-239). */
 TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dtype, const int8_t* int8_tiles,
@@ -141,7 +142,7 @@ TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dt
 
 /* Launch geometry the decode kernels use when split_k = 0 on this device: *split
  * (1..16) and *rows_per_cta (row tiles one CTA streams when split is 1).  Up to 16 rows
- * (without fused quantization) this is the split of TQ_ALGO_STREAM: the most splits (at
+ * (with or without fused quantization) this is the split of TQ_ALGO_STREAM: the most splits (at
  * most 8, at least 4 INT8 tiles each) whose n_tr clusters of split CTAs are all resident
  * on this device at once, 1 if none is; the automatic choice also gives it to the row
  * kernel when the stream kernel cannot take a call.  Otherwise the split of the row

@@ -110,3 +110,20 @@ def test_auto_falls_back_to_row_kernel_at_the_same_split(cuda_device):
     auto = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, **_kw(p, m, k, None))
     rows_y = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, algo=N.TQ_ALGO_ROWS, **_kw(p, m, k, split))
     assert torch.equal(auto.view(torch.int16), rows_y.view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,m,k,keep", [(4, 3072, 3072, 0.01), (16, 640, 1024, 0.1), (1, 5120, 3072, 0.0),
+                                           (9, 3072, 8192, 0.05), (16, 192, 4160, 0.3)])
+def test_fused_quant_stream_identical_to_two_steps(cuda_device, dtype, rows, m, k, keep):
+    """The quantizer inside the stream kernel: the same bits as quantize + GEMM."""
+    x = (I.activations(rows, k, 740 + rows, outliers=3).to(DEV) * 3).to(dtype)
+    w = I.weight(m, k, 741).to(dtype)
+    n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
+    p, _ = _pack(w, n_tr, n_tc, keep, 742)
+    b = I.weight(1, m, 743, std=0.3).reshape(-1).to(DEV).to(dtype)
+    kw = _kw(p, m, k, None, b, dtype)
+    q, sx = tq.quantize_activation_tile_absmax(x)
+    two = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, **kw)
+    one = tq.gemm_mixed_fused_quant(x_fp=x, **kw)
+    assert torch.equal(one.view(torch.int16), two.view(torch.int16))

@@ -530,14 +530,19 @@ template <int XT>
 static int launch_norm(int nvt, const void* resid, int64_t ld_r, const void* delta, int64_t ld_d, const void* weight,
                        void* resid_out, int64_t ld_ro, void* y, int64_t ld_y, int64_t n_rows, int H, float eps,
                        cudaStream_t st) {
-  const unsigned g = (unsigned)n_rows;
-  switch (nvt) {
-    case 1: add_rmsnorm_kernel<XT, 1><<<g, 256, 0, st>>>(resid, ld_r, delta, ld_d, weight, resid_out, ld_ro, y, ld_y, H, eps); break;
-    case 2: add_rmsnorm_kernel<XT, 2><<<g, 256, 0, st>>>(resid, ld_r, delta, ld_d, weight, resid_out, ld_ro, y, ld_y, H, eps); break;
-    case 4: add_rmsnorm_kernel<XT, 4><<<g, 256, 0, st>>>(resid, ld_r, delta, ld_d, weight, resid_out, ld_ro, y, ld_y, H, eps); break;
-    default: add_rmsnorm_kernel<XT, 8><<<g, 256, 0, st>>>(resid, ld_r, delta, ld_d, weight, resid_out, ld_ro, y, ld_y, H, eps); break;
-  }
-  TQ_LAUNCHED();
+  auto kern = nvt == 1 ? add_rmsnorm_kernel<XT, 1>
+                       : nvt == 2 ? add_rmsnorm_kernel<XT, 2> : nvt == 4 ? add_rmsnorm_kernel<XT, 4> : add_rmsnorm_kernel<XT, 8>;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)n_rows, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = tq_pdl_enabled() ? 1 : 0;
+  TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, resid, ld_r, delta, ld_d, weight, resid_out, ld_ro, y, ld_y, H, eps));
+  tq_count_launch();
   return TQ_OK;
 }
 

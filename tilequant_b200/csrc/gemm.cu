@@ -184,6 +184,12 @@ extern "C" int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int f
   a.split = split_k;
   a.has_fp16 = t16 > 0;
   a.fused = 1;
+  a.w8_rows = t8 * 64;
+  a.w16_rows = t16 * 64;
+  if (n_rows <= 16) {  // decode: the stream kernel quantizes in its prologue; else the row kernel at its split
+    if (a.split == 0) a.split = tq_stream_split(n_tr, n_tc, (int)n_rows);
+    if (tq_stream_supported(a)) return tq_launch_stream(a, n_tr, fp_dtype, (cudaStream_t)stream);
+  }
   return tq_launch_rows(a, n_tr, fp_dtype, (cudaStream_t)stream, t16);
 }
 

@@ -581,7 +581,7 @@ int tq_stream_split(int n_tr, int n_tc, int n_rows);
 
 extern "C" int tq_gemm_rows_plan(int64_t n_rows, int n_tr, int n_tc, int fp_dtype, int fused, int* split, int* rows_per_cta) {
   if (n_rows <= 0 || n_tr <= 0 || n_tc <= 0 || !split || !rows_per_cta) return tq_set_error(TQ_ERR_INVALID, "bad plan query");
-  if (n_rows <= 16 && !fused) {  // the stream decode kernel (TQ_ALGO_STREAM), or the row kernel at its split
+  if (n_rows <= 16) {  // the stream decode kernel (TQ_ALGO_STREAM), or the row kernel at its split
     *split = tq_stream_split(n_tr, n_tc, (int)n_rows);
     *rows_per_cta = 1;
     return TQ_OK;

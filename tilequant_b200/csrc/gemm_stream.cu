@@ -25,7 +25,9 @@
 //     so the weight stream starts while that kernel finishes;
 //   * the INT8 activations of the split's column range are copied into shared memory
 //     once (one bulk copy per row, rows padded so the operand loads are free of bank
-//     conflicts) and stay there; each 16-bit tile arrives as an 8 KB bulk copy plus a TMA box of
+//     conflicts) and stay there; with fused quantization the consumers make those
+//     codes and scales from the 16-bit activations instead, bit-identical to the
+//     activation quantizer (one launch instead of two); each 16-bit tile arrives as an 8 KB bulk copy plus a TMA box of
 //     its 16-bit activation columns, in a separate one-slot ring;
 //   * four consumer warps split every tile by weight rows (warp w: rows 16w..16w+15,
 //     swap-AB mma.sync m16n8k32 with the k order permuted identically for both
@@ -117,6 +119,67 @@ __host__ __device__ constexpr int stream_chunks(int n_rows, int K, int n_tc) {
   return n < 2 ? 2 : (n > sk::MAX_NCH ? sk::MAX_NCH : n);
 }
 
+// Fused activation quantization (the consumers, after the wait): column tiles
+// [c_lo, c_hi) of the 16-bit activations, all n_rows rows, become INT8 codes in `act`
+// (row stride act_ld, column c at (c - c_lo) * 64) and scales in sxs[c], exactly as the
+// activation quantizer makes them: scale = dtype(absmax / 127) over the tile's rows
+// and columns, code = rint(x / scale) clamped (quantize.cu).  Warp w takes tiles
+// c_lo + w, c_lo + w + 4, ...; lane l reads the 16-byte piece l % 8 of rows l / 8,
+// l / 8 + 4, ...; up to four tiles' loads are in flight at once.
+template <int XT>
+__device__ __forceinline__ void quantize_columns(const RowsArgs& a, int8_t* act, int act_ld, float* sxs, int c_lo,
+                                                 int c_hi, int warp, int lane) {
+  constexpr int GRP = 4, RPL = 4;  // tiles per group, rows per lane (16 rows / 4)
+  const int piece = lane & 7, r0 = lane >> 3;
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(a.x_fp);
+  for (int c0 = c_lo + warp; c0 < c_hi; c0 += GRP * sk::CONS) {
+    uint4 v[GRP][RPL];
+#pragma unroll
+    for (int gi = 0; gi < GRP; ++gi) {
+      const int c = c0 + gi * sk::CONS, col = c * 64 + piece * 8;
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const int row = r0 + 4 * k;
+        v[gi][k] = (c < c_hi && row < a.n_rows && col < a.K)
+                       ? *reinterpret_cast<const uint4*>(x + (int64_t)row * a.ld_xfp + col)
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int gi = 0; gi < GRP; ++gi) {
+      const int c = c0 + gi * sk::CONS;
+      if (c >= c_hi) break;  // warp-uniform
+      float m = 0.0f;
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const uint32_t w4[4] = {v[gi][k].x, v[gi][k].y, v[gi][k].z, v[gi][k].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          m = fmaxf(m, fmaxf(fabsf(h2f((uint16_t)(w4[e] & 0xffffu), XT)), fabsf(h2f((uint16_t)(w4[e] >> 16), XT))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float sc = scale_from_absmax<XT>(m);
+      const float rc = __frcp_rn(sc);
+#pragma unroll
+      for (int k = 0; k < RPL; ++k) {
+        const int row = r0 + 4 * k;
+        if (row >= a.n_rows) continue;
+        const uint32_t w4[4] = {v[gi][k].x, v[gi][k].y, v[gi][k].z, v[gi][k].w};
+        uint32_t o2[2] = {0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int lo = quant_code_fast(h2f((uint16_t)(w4[e] & 0xffffu), XT), sc, rc);
+          const int hi = quant_code_fast(h2f((uint16_t)(w4[e] >> 16), XT), sc, rc);
+          o2[e >> 1] |= ((uint32_t)(lo & 0xff) | ((uint32_t)(hi & 0xff) << 8)) << ((e & 1) * 16);
+        }
+        *reinterpret_cast<uint2*>(act + row * act_ld + (c - c_lo) * 64 + piece * 8) = make_uint2(o2[0], o2[1]);
+      }
+      if (lane == 0) sxs[c] = sc;
+    }
+  }
+}
+
 template <int NB, int XT>
 __global__ void __launch_bounds__(sk::THREADS) stream_kernel(const RowsArgs a, const __grid_constant__ StreamMaps maps) {
   using namespace sk;
@@ -201,8 +264,8 @@ __global__ void __launch_bounds__(sk::THREADS) stream_kernel(const RowsArgs a, c
     const uint32_t span = (uint32_t)(n8 ? min(c_end * 64, K) - c_first * 64 : 0);
     grid_dep_wait();  // activations come from the preceding kernel
     if (leader) {
-      mbar_expect_tx(&act_bar, (uint32_t)a.n_rows * span);
-      if (span)
+      mbar_expect_tx(&act_bar, a.fused ? 0u : (uint32_t)a.n_rows * span);
+      if (span && !a.fused)
         for (int row = 0; row < a.n_rows; ++row)
           bulk_g2s(act + row * act_ld, a.x_i8 + (int64_t)row * a.ld_x8 + c_first * 64, span, &act_bar);
       for (int j = 0; j < min(NS16, n16); ++j) issue16_x(j);
@@ -227,8 +290,12 @@ __global__ void __launch_bounds__(sk::THREADS) stream_kernel(const RowsArgs a, c
       mcol[i] = __ldg(a.ids8 + lo8 + i) % n_tc - c_first;
       msw[i] = a.s8 ? __ldg(a.s8 + lo8 + i) : 1.0f;
     }
-    grid_dep_wait();  // scales come from the preceding kernel, which may also still read `out`
-    for (int c = tid; c < n_tc; c += CONS * 32) sxs[c] = a.sx ? __ldg(a.sx + c) : 1.0f;
+    grid_dep_wait();  // activations come from the preceding kernel, which may also still read `out`
+    if (a.fused) {
+      if (n8) quantize_columns<XT>(a, act, act_ld, sxs, c_first, __ldg(a.ids8 + lo8 + n8 - 1) % n_tc + 1, warp, lane);
+    } else {
+      for (int c = tid; c < n_tc; c += CONS * 32) sxs[c] = a.sx ? __ldg(a.sx + c) : 1.0f;
+    }
     named_bar_sync(1, CONS * 32);
     ok = mbar_wait_bounded(&act_bar, 0, a.err);
 
@@ -408,16 +475,17 @@ int tq_stream_split(int n_tr, int n_tc, int n_rows) {
   return best;
 }
 
-// Whether the stream kernel takes this call: <= 16 rows, split 1..8, 16-byte aligned
-// INT8 activation rows of a multiple of 16 values, 16-bit activation rows a tensor map
-// can address, and the activations fitting in shared memory with the rings.
+// Whether the stream kernel takes this call: <= 16 rows, split 1..8, K a multiple of 16,
+// 16-byte aligned INT8 activation rows (or, with fused quantization, 16-bit ones), 16-bit
+// activation rows a tensor map can address, and the activations fitting in shared
+// memory with the rings.
 int tq_stream_supported(const RowsArgs& a) {
-  if (a.n_rows <= 0 || a.n_rows > 16 || a.partials || a.fused) return 0;
-  if (a.split < 0 || a.split > sk::MAX_S) return 0;
-  if (!a.x_i8 || ((uintptr_t)a.x_i8 & 15) || (a.ld_x8 & 15) || (a.K & 15)) return 0;
-  if (a.has_fp16 && (!a.x_fp || ((uintptr_t)a.x_fp & 15) || ((a.ld_xfp * 2) & 15) || ((uintptr_t)a.w16 & 15) ||
-                     a.K < 64))
-    return 0;
+  if (a.n_rows <= 0 || a.n_rows > 16 || a.partials) return 0;
+  if (a.split < 0 || a.split > sk::MAX_S || (a.K & 15)) return 0;
+  if (!a.fused && (!a.x_i8 || ((uintptr_t)a.x_i8 & 15) || (a.ld_x8 & 15))) return 0;
+  const bool need_fp = a.has_fp16 || a.fused;  // the 16-bit activations are read (TMA box / quantizer)
+  if (need_fp && (!a.x_fp || ((uintptr_t)a.x_fp & 15) || ((a.ld_xfp * 2) & 15))) return 0;
+  if (a.has_fp16 && (((uintptr_t)a.w16 & 15) || a.K < 64)) return 0;
   return stream_smem(a.n_rows, a.K, a.n_tc, stream_chunks(a.n_rows, a.K, a.n_tc)) <= 227 * 1024;
 }
 

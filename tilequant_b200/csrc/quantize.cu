@@ -143,6 +143,7 @@ template <int XT>
 __global__ void __launch_bounds__(256) quantize_small_kernel(const void* __restrict__ x, int64_t n_rows, int64_t k,
                                                              int64_t ld_row, int64_t ld_col, int8_t* __restrict__ q,
                                                              int64_t ldq, float* __restrict__ sx) {
+  grid_dep_wait();  // x comes from the preceding kernel (launched with programmatic serialization)
   grid_dep_launch();
   __shared__ float tile[128 * 64];
   __shared__ float red[32];
@@ -261,11 +262,20 @@ extern "C" int tq_quantize_act(const void* x, int x_dtype, int64_t n_rows, int64
   cudaStream_t st = (cudaStream_t)stream;
   if (n_rows <= 128) {
     const int n_tc = (int)((k + 63) / 64);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)n_tc, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = tq_pdl_enabled() ? 1 : 0;
     if (x_dtype == TQ_DTYPE_BF16)
-      quantize_small_kernel<TQ_DTYPE_BF16><<<n_tc, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, q, ldq, sx);
+      TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_small_kernel<TQ_DTYPE_BF16>, x, n_rows, k, ld_row, ld_col, q, ldq, sx));
     else
-      quantize_small_kernel<TQ_DTYPE_F16><<<n_tc, 256, 0, st>>>(x, n_rows, k, ld_row, ld_col, q, ldq, sx);
-    TQ_LAUNCHED();
+      TQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, quantize_small_kernel<TQ_DTYPE_F16>, x, n_rows, k, ld_row, ld_col, q, ldq, sx));
+    tq_count_launch();
     return TQ_OK;
   }
   rc = launch_scales(x, x_dtype, n_rows, k, ld_row, ld_col, sx, st);

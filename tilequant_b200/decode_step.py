@@ -251,6 +251,10 @@ class FusedDecodeStep:
         self.h_q = torch.empty((B, inter), device=dev, dtype=torch.int8)
         self.h_sx = torch.empty(((inter + 63) // 64,), device=dev, dtype=torch.float32)
 
+    def _norm(self, resid, delta, weight, eps):
+        """The layer input: residual add (with delta) and RMSNorm."""
+        return add_rmsnorm(resid, delta, weight, eps, resid_out=self.resid, out=self.x), None, None
+
     def status(self) -> int:
         """The attention kernel's error word (0, or TQ_ERR_TIMEOUT); synchronises."""
         return int(self.ws.err.item())
@@ -265,12 +269,12 @@ class FusedDecodeStep:
         cos, sin = cos.reshape(-1), sin.reshape(-1)
         resid, delta = emb, None
         for L in self.layers:
-            # residual add (from the second layer on) + input RMSNorm
-            x = add_rmsnorm(resid, delta, L.norm1.weight, L.eps1, resid_out=self.resid, out=self.x)
+            # residual add (from the second layer on) + input RMSNorm (+ the QKV input's codes)
+            x, xq, xsx = self._norm(resid, delta, L.norm1.weight, L.eps1)
             resid = self.resid if delta is not None else resid
             qd, kd = L.Hq * L.D, L.Hkv * L.D
             if L.qkv is not None:
-                y = _proj(L.qkv, x)
+                y = _proj(L.qkv, x, xq, xsx)
                 q, k, v = y[:, :qd], y[:, qd:qd + kd], y[:, qd + kd:qd + 2 * kd]
             else:
                 q, k, v = _proj(L.q_proj, x), _proj(L.k_proj, x), _proj(L.v_proj, x)
@@ -278,10 +282,10 @@ class FusedDecodeStep:
             attn_decode(q, k, v, cos, sin, L.k_cache, L.v_cache, position, L.scale, self.ws, out=a_out, q_out=a_q,
                         sx=a_sx)
             delta = _proj(L.o_proj, a_out, a_q, a_sx)
-            x = add_rmsnorm(resid, delta, L.norm2.weight, L.eps2, resid_out=self.resid, out=self.x)
+            x, xq, xsx = self._norm(resid, delta, L.norm2.weight, L.eps2)
             resid = self.resid
             if L.gate_up is not None:
-                gu = _proj(L.gate_up, x)
+                gu = _proj(L.gate_up, x, xq, xsx)
                 gate, up = gu[:, :L.inter], gu[:, L.inter:2 * L.inter]
             else:
                 gate, up = _proj(L.gate_proj, x), _proj(L.up_proj, x)
