@@ -55,12 +55,14 @@ enum {
                         (DSMEM) split reduction; decode and general fallback      */
   TQ_ALGO_UMMA = 2,  /* persistent TMA + tcgen05 (kind::i8 / kind::f16) kernel    */
   TQ_ALGO_GEMV = 3,  /* decode kernel: operands straight into MMA fragments, split-K
-                        across the warps of a CTA; by name, up to 64 rows (16-row
-                        blocks); the form the row-parallel peer sum uses         */
+                        across the warps of a CTA; chosen automatically for 9..16
+                        rows when its grid fits one wave and each warp holds few
+                        tiles, by name for up to 64 rows (16-row blocks); the form
+                        the row-parallel peer sum uses                           */
   TQ_ALGO_STREAM = 4 /* decode kernel for <= 16 rows: one CTA per (split, row tile),
                         the splits of a row tile a cluster (DSMEM reduction), INT8
                         tiles in 16 KB bulk copies, activations resident in shared
-                        memory; the automatic choice for <= 16 rows where it fits,
+                        memory; the automatic choice for <= 8 rows where it fits,
                         else the row kernel at the same split                    */
 };
 
@@ -130,7 +132,7 @@ TQ_API int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx, con
 
 /* Decode form with the activation quantizer fused into the GEMM prologue: the same
  * result as tq_quantize_act followed by tq_gemm_mixed, in one launch.  n_rows <= 64; up
- * to 16 rows it runs the stream kernel, whose splits each quantize their own columns.
+ * to 8 rows it runs the stream kernel, whose splits each quantize their own columns.
  * replaces quantize_activation_tile_absmax + gemm_mixed_rows_splitk as called by
  * MixedLinear.forward for small row counts (src/models/mixed_linear.py:232-239). */
 TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dtype, const int8_t* int8_tiles,
@@ -142,11 +144,13 @@ TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dt
 
 /* Launch geometry the decode kernels use when split_k = 0 on this device: *split
  * (1..16) and *rows_per_cta (row tiles one CTA streams when split is 1).  Up to 16 rows
- * (with or without fused quantization) this is the split of TQ_ALGO_STREAM: the most splits (at
- * most 8, at least 4 INT8 tiles each) whose n_tr clusters of split CTAs are all resident
- * on this device at once, 1 if none is; the automatic choice also gives it to the row
- * kernel when the stream kernel cannot take a call.  Otherwise the split of the row
- * kernel (TQ_ALGO_ROWS).
+ * Up to 8 rows (with or without fused quantization) this is the split of TQ_ALGO_STREAM:
+ * the most splits (at most 8, at least 4 INT8 tiles each) whose n_tr clusters of split
+ * CTAs are all resident on this device at once, 1 if none is; the automatic choice also
+ * gives it to the row kernel when the stream kernel cannot take a call.  For 9..16 rows
+ * it is the split of TQ_ALGO_GEMV where the automatic choice takes that kernel (its grid
+ * fits one wave and each warp holds few tiles).  Otherwise the split of the row kernel
+ * (TQ_ALGO_ROWS).
  * The split fixes the FP32 summation order of the result; passing it back as split_k
  * reproduces the same result.  (The reference picks its split from a fixed rule,
  * select_split_k, gemm_rows_splitk_64x64.py:52-67; this one sizes the grid to one

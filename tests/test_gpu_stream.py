@@ -82,8 +82,9 @@ def test_stream_identical_to_row_kernel(cuda_device, dtype, rows, m, k, keep, sp
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
-@pytest.mark.parametrize("rows,m,k", [(4, 3072, 3072), (16, 16384, 3072), (1, 3072, 8192)])
+@pytest.mark.parametrize("rows,m,k", [(4, 3072, 3072), (8, 16384, 3072), (1, 3072, 8192)])
 def test_auto_is_stream_at_the_planned_split(cuda_device, rows, m, k):
+    """Up to 8 rows the automatic choice is this kernel at select_split_k's split."""
     x = I.activations(rows, k, 720 + rows, outliers=2).to(DEV)
     w = I.weight(m, k, 721)
     n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
@@ -116,13 +117,15 @@ def test_auto_falls_back_to_row_kernel_at_the_same_split(cuda_device):
 @pytest.mark.parametrize("rows,m,k,keep", [(4, 3072, 3072, 0.01), (16, 640, 1024, 0.1), (1, 5120, 3072, 0.0),
                                            (9, 3072, 8192, 0.05), (16, 192, 4160, 0.3)])
 def test_fused_quant_stream_identical_to_two_steps(cuda_device, dtype, rows, m, k, keep):
-    """The quantizer inside the stream kernel: the same bits as quantize + GEMM."""
+    """The quantizer inside the GEMM launch (the stream kernel up to 8 rows, the row kernel
+    beyond): the same bits as quantize + GEMM at the same split."""
     x = (I.activations(rows, k, 740 + rows, outliers=3).to(DEV) * 3).to(dtype)
     w = I.weight(m, k, 741).to(dtype)
     n_tr, n_tc = (m + 63) // 64, (k + 63) // 64
     p, _ = _pack(w, n_tr, n_tc, keep, 742)
     b = I.weight(1, m, 743, std=0.3).reshape(-1).to(DEV).to(dtype)
-    kw = _kw(p, m, k, None, b, dtype)
+    split = tq.select_split_k(n_tr=n_tr, n_tc=n_tc, n_rows=rows, device=torch.device(DEV), dtype=dtype, fused=True)
+    kw = _kw(p, m, k, split, b, dtype)
     q, sx = tq.quantize_activation_tile_absmax(x)
     two = tq.gemm_mixed_rows_splitk(x_fp=x, x_int8=q, sx=sx, **kw)
     one = tq.gemm_mixed_fused_quant(x_fp=x, **kw)

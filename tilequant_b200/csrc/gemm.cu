@@ -99,15 +99,15 @@ extern "C" int tq_gemm_mixed(const int8_t* x_i8, int64_t ld_x8, const float* sx,
       return tq_set_error(TQ_ERR_UNSUPPORTED, "tcgen05 GEMM: unsupported shape or alignment");
     return tq_launch_umma(a, n_tr, fp_dtype, st);
   }
-  if (algo == TQ_ALGO_STREAM || (algo == TQ_ALGO_AUTO && n_rows <= 16)) {
-    // decode: the stream kernel at its split; where it cannot take the call (alignment,
-    // shared memory), the row kernel at the same split gives the same bits
+  if (algo == TQ_ALGO_STREAM || (algo == TQ_ALGO_AUTO && n_rows <= 8)) {
+    // decode up to 8 rows: the stream kernel at its split; where it cannot take the call
+    // (alignment, shared memory), the row kernel at the same split gives the same bits
     if (a.split == 0) a.split = tq_stream_split(n_tr, n_tc, (int)n_rows);
     if (tq_stream_supported(a)) return tq_launch_stream(a, n_tr, fp_dtype, st);
     if (algo == TQ_ALGO_STREAM) return tq_set_error(TQ_ERR_UNSUPPORTED, "stream decode kernel: unsupported call");
     return tq_launch_rows(a, n_tr, fp_dtype, st, t16);
   }
-  if (algo == TQ_ALGO_GEMV) {
+  if (algo == TQ_ALGO_GEMV || (algo == TQ_ALGO_AUTO && tq_gemv_preferred(a, n_tr))) {
     // asked for by name, the decode kernel also runs 17..64 rows as 16-row blocks
     if (!tq_gemv_peer_supported(a))
       return tq_set_error(TQ_ERR_UNSUPPORTED, "decode kernel: needs <= 64 rows and split_k <= 8");
@@ -186,7 +186,7 @@ extern "C" int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int f
   a.fused = 1;
   a.w8_rows = t8 * 64;
   a.w16_rows = t16 * 64;
-  if (n_rows <= 16) {  // decode: the stream kernel quantizes in its prologue; else the row kernel at its split
+  if (n_rows <= 8) {  // decode: the stream kernel quantizes in its prologue; else the row kernel at its split
     if (a.split == 0) a.split = tq_stream_split(n_tr, n_tc, (int)n_rows);
     if (tq_stream_supported(a)) return tq_launch_stream(a, n_tr, fp_dtype, (cudaStream_t)stream);
   }

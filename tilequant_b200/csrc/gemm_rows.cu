@@ -578,13 +578,25 @@ int tq_launch_rows(RowsArgs& a, int n_tr, int fp_dtype, cudaStream_t st, int64_t
 
 // The split and row tiles per CTA the rows kernel picks for a shape (split_k = 0).
 int tq_stream_split(int n_tr, int n_tc, int n_rows);
+int tq_gemv_split(int n_tc);
+int tq_gemv_preferred(const tq::RowsArgs& a, int n_tr);
 
 extern "C" int tq_gemm_rows_plan(int64_t n_rows, int n_tr, int n_tc, int fp_dtype, int fused, int* split, int* rows_per_cta) {
   if (n_rows <= 0 || n_tr <= 0 || n_tc <= 0 || !split || !rows_per_cta) return tq_set_error(TQ_ERR_INVALID, "bad plan query");
-  if (n_rows <= 16) {  // the stream decode kernel (TQ_ALGO_STREAM), or the row kernel at its split
+  if (n_rows <= 8) {  // the stream decode kernel (TQ_ALGO_STREAM), or the row kernel at its split
     *split = tq_stream_split(n_tr, n_tc, (int)n_rows);
     *rows_per_cta = 1;
     return TQ_OK;
+  }
+  if (n_rows <= 16 && !fused) {  // the register-fragment decode kernel (TQ_ALGO_GEMV) where it is chosen
+    tq::RowsArgs a = {};
+    a.n_rows = (int)n_rows;
+    a.n_tc = n_tc;
+    if (tq_gemv_preferred(a, n_tr)) {
+      *split = tq_gemv_split(n_tc);
+      *rows_per_cta = 1;
+      return TQ_OK;
+    }
   }
   const int nb = rows_nb(n_rows);
   const int n_blocks = (int)((n_rows + 8 * nb - 1) / (8 * nb));
