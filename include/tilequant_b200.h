@@ -284,7 +284,8 @@ TQ_API int tq_silu_mul_quant(const void* gate, const void* up, int64_t ld_gu, in
 
 /* One query token per sequence against a head-major KV cache [B][Hkv][L][D]
  * (16-byte aligned, contiguous).  q/k/v: the projections' outputs for the token (row
- * b, head h at + b * ld + h * D).  The kernel applies RoPE (cos/sin: D values of the
+ * b, head h at + b * ld + h * D; every row, and cos/sin, on 16-byte boundaries).  The
+ * kernel applies RoPE (cos/sin: D values of the
  * current position) to q and k, writes the rotated k and v into cache slot *pos, and
  * attends over slots [0, *pos] in S splits (ws_*: f32 scratch of B*Hq*S, B*Hq*S,
  * B*Hq*S*D); *pos is read on the device, so one launch serves every step of a graph. */

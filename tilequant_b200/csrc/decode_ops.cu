@@ -203,6 +203,35 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
 __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int c) {
   return base + (uint32_t)((c >> 3) * at::BOXB + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
+// 8 rotated values d0..d0+7 of one head x[0..D) (16-byte aligned pieces):
+// round(round(x * cos) + round(rotate_half(x) * sin)), rotate_half(x)[d] = -x[d + D/2]
+// for d < D/2 and x[d - D/2] above.
+template <int XT>
+__device__ __forceinline__ uint4 rope8(const uint16_t* x, int d0, int D, const void* cosp, const void* sinp) {
+  const bool lower = d0 < D / 2;
+  const uint4 xv = *reinterpret_cast<const uint4*>(x + d0);
+  const uint4 rv = *reinterpret_cast<const uint4*>(x + (lower ? d0 + D / 2 : d0 - D / 2));
+  const uint4 cv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(cosp) + d0);
+  const uint4 sv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(sinp) + d0);
+  const uint32_t x4[4] = {xv.x, xv.y, xv.z, xv.w}, r4[4] = {rv.x, rv.y, rv.z, rv.w};
+  const uint32_t c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
+  uint32_t o4[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float o[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float xx = h2f((uint16_t)(x4[e] >> (16 * h)), XT);
+      float rr = h2f((uint16_t)(r4[e] >> (16 * h)), XT);
+      if (lower) rr = -rr;
+      const float cc = h2f((uint16_t)(c4[e] >> (16 * h)), XT), ss = h2f((uint16_t)(s4[e] >> (16 * h)), XT);
+      o[h] = round16(__fadd_rn(round16(__fmul_rn(xx, cc), XT), round16(__fmul_rn(rr, ss), XT)), XT);
+    }
+    o4[e] = (uint32_t)f2h(o[0], XT) | ((uint32_t)f2h(o[1], XT) << 16);
+  }
+  return make_uint4(o4[0], o4[1], o4[2], o4[3]);
+}
+
 template <int XT>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return (uint32_t)f2h(lo, XT) | ((uint32_t)f2h(hi, XT) << 16);
@@ -258,31 +287,28 @@ __global__ void __launch_bounds__(at::WARPS * 32) attn_partial_kernel(const Attn
   grid_dep_launch();
 
   // RoPE of the query heads: round(round(q * cos) + round(rotate_half(q) * sin)) (the
-  // decoder's apply_rotary_pos_emb, op by op); rows G..7 zero
-  for (int e = tid; e < MAXG * D; e += blockDim.x) {
-    const int hh = e / D, d = e % D;
-    float v = 0.0f;
+  // decoder's apply_rotary_pos_emb, op by op); rows G..7 zero.  One 16-byte piece (8
+  // values, all in one half of the head) per thread: every load in one round.
+  for (int pc = tid; pc < MAXG * D / 8; pc += blockDim.x) {
+    const int hh = pc / (D / 8), d0 = (pc % (D / 8)) * 8;
+    uint4 outv = make_uint4(0u, 0u, 0u, 0u);
     if (hh < G) {
       const int64_t base = (int64_t)b * a.ld_q + (int64_t)(kvh * G + hh) * D;
-      const float x = ldh<XT>(a.q, base + d);
-      const float r = d < D / 2 ? -ldh<XT>(a.q, base + d + D / 2) : ldh<XT>(a.q, base + d - D / 2);
-      v = round16(__fadd_rn(round16(__fmul_rn(x, ldh<XT>(a.cos, d)), XT), round16(__fmul_rn(r, ldh<XT>(a.sin, d)), XT)),
-                  XT);
+      outv = rope8<XT>(reinterpret_cast<const uint16_t*>(a.q) + base, d0, D, a.cos, a.sin);
     }
-    qh[e] = f2h(v, XT);
+    *reinterpret_cast<uint4*>(qh + hh * D + d0) = outv;
   }
   // the split holding slot pos writes the new token's rotated K and its V there; its
   // TMA loads of that chunk read them after the proxy fence and the barrier
   if (pos_chunk >= 0) {
     const int64_t kb = (int64_t)b * a.ld_k + (int64_t)kvh * D, vb = (int64_t)b * a.ld_v + (int64_t)kvh * D;
     const int64_t dst = ((int64_t)row0 + pos) * D;
-    for (int d = tid; d < D; d += blockDim.x) {
-      const float x = ldh<XT>(a.k, kb + d);
-      const float r = d < D / 2 ? -ldh<XT>(a.k, kb + d + D / 2) : ldh<XT>(a.k, kb + d - D / 2);
-      sth<XT>(a.k_cache, dst + d,
-              round16(__fadd_rn(round16(__fmul_rn(x, ldh<XT>(a.cos, d)), XT),
-                                round16(__fmul_rn(r, ldh<XT>(a.sin, d)), XT)), XT));
-      reinterpret_cast<uint16_t*>(a.v_cache)[dst + d] = reinterpret_cast<const uint16_t*>(a.v)[vb + d];
+    for (int pc = tid; pc < D / 8; pc += blockDim.x) {
+      const int d0 = pc * 8;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.k_cache) + dst + d0) =
+          rope8<XT>(reinterpret_cast<const uint16_t*>(a.k) + kb, d0, D, a.cos, a.sin);
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.v_cache) + dst + d0) =
+          *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.v) + vb + d0);
     }
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
@@ -635,6 +661,9 @@ extern "C" int tq_attn_decode(const AttnArgs* args, void* out, int64_t ld_out, i
     return tq_set_error(TQ_ERR_INVALID, "null pointer");
   if ((((uintptr_t)a.k_cache) | ((uintptr_t)a.v_cache)) & 15)
     return tq_set_error(TQ_ERR_INVALID, "KV cache must be 16-byte aligned");
+  if ((((uintptr_t)a.q) | ((uintptr_t)a.k) | ((uintptr_t)a.v) | ((uintptr_t)a.cos) | ((uintptr_t)a.sin)) & 15 ||
+      ((a.ld_q | a.ld_k | a.ld_v) & 7))
+    return tq_set_error(TQ_ERR_INVALID, "q, k, v, cos and sin must start (and their rows) on 16-byte boundaries");
   if (ld_out < (int64_t)a.Hq * a.D || (q_out && (!sx || ldq < (int64_t)a.Hq * a.D)))
     return tq_set_error(TQ_ERR_INVALID, "bad output stride or quantized output");
   const uint64_t rows = (uint64_t)a.B * a.Hkv * a.L;
