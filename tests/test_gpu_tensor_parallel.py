@@ -6,7 +6,10 @@ through the peer sum against the unsplit GEMM."""
 
 from __future__ import annotations
 
+import queue
 import socket
+import time
+import traceback
 
 import pytest
 import torch
@@ -19,6 +22,48 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _guarded(target, rank, world, port, out_q, *args):
+    """Run one rank's `target`; its result, or the traceback of what it raised, goes to
+    `out_q` as (rank, ok, payload) so the parent learns of a failed rank at once."""
+    try:
+        out_q.put((rank, True, target(rank, world, port, *args)))
+    except BaseException:
+        out_q.put((rank, False, traceback.format_exc()))
+        raise
+
+
+def _run_two_ranks(target, *args, deadline_s=400):
+    """Spawn two ranks of `target(rank, world, port, *args)` and return their results in
+    rank order.  A rank that raised fails the test with its traceback as soon as it is
+    reported; ranks are never killed (the one still in a collective ends on its process
+    group's timeout), and the parent waits no longer than `deadline_s` for results."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_guarded, args=(target, r, 2, port, q) + args) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    end = time.monotonic() + deadline_s
+    while len(res) < 2 and time.monotonic() < end:
+        try:
+            rank, ok, payload = q.get(timeout=1.0)
+        except queue.Empty:
+            if all(p.exitcode is not None for p in procs):
+                break
+            continue
+        res[rank] = (ok, payload)
+        if not ok:
+            break
+    for p in procs:
+        p.join(timeout=180)
+    failed = {r: v[1] for r, v in res.items() if not v[0]}
+    assert not failed, "\n".join(f"rank {r}:\n{tb}" for r, tb in failed.items())
+    assert len(res) == 2, f"ranks without a result (exit codes {[p.exitcode for p in procs]})"
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return [res[r][1] for r in range(2)]
 
 
 def _model(dev, qwen=False):
@@ -37,7 +82,7 @@ def _model(dev, qwen=False):
         return Model(cfg).to(torch.bfloat16).eval()
 
 
-def _worker(rank, world, port, qwen, peer, out_q):
+def _worker(rank, world, port, qwen, peer):
     import os
 
     import torch.distributed as dist
@@ -79,7 +124,7 @@ def _worker(rank, world, port, qwen, peer, out_q):
         dist.all_gather(gathered, toks)
         same = all(torch.equal(g, toks) for g in gathered)
         status = 0 if exchange is None else exchange.status()
-        out_q.put((rank, rel, agree, same, status))
+        return rel, agree, same, status
     finally:
         if exchange is not None:
             torch.cuda.synchronize()
@@ -92,17 +137,8 @@ def _worker(rank, world, port, qwen, peer, out_q):
 def test_tensor_parallel_two_gpus(qwen, peer):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, qwen, peer, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=600) for _ in procs]
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    for rank, rel, agree, same, status in res:
+    res = _run_two_ranks(_worker, qwen, peer)
+    for rank, (rel, agree, same, status) in enumerate(res):
         # row-parallel partials are summed in another order than the single-GPU K loop
         # (and rounded to BF16 first on the NCCL path), and the difference travels
         # through every later layer in BF16
@@ -112,7 +148,7 @@ def test_tensor_parallel_two_gpus(qwen, peer):
         assert status == 0, rank  # no peer wait ran out
 
 
-def _gemm_worker(rank, world, port, out_q):
+def _gemm_worker(rank, world, port):
     import datetime
     import os
     from types import SimpleNamespace
@@ -177,7 +213,7 @@ def _gemm_worker(rank, world, port, out_q):
                 gathered = [torch.empty_like(got) for _ in range(world)]
                 dist.all_gather(gathered, got)
                 same = same and all(torch.equal(g.view(torch.int16), got.view(torch.int16)) for g in gathered)
-        out_q.put((rank, errors, same, exchange.status()))
+        return errors, same, exchange.status()
     finally:
         torch.cuda.synchronize()
         dist.barrier()
@@ -188,23 +224,14 @@ def _gemm_worker(rank, world, port, out_q):
 def test_peer_sum_gemm_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_gemm_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=600) for _ in procs]
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    for rank, errors, same, status in res:
+    res = _run_two_ranks(_gemm_worker)
+    for rank, (errors, same, status) in enumerate(res):
         assert status == 0, rank
         assert same, rank  # the same bits on every rank
         assert not errors, (rank, errors)
 
 
-def _token_worker(rank, world, port, name, peer, out_q):
+def _token_worker(rank, world, port, name, peer):
     """TP1 (this GPU alone) against TP2 on the greedy-token fixture models: TP1 decodes
     freely, TP2 is teacher-forced on TP1's tokens."""
     import datetime
@@ -248,7 +275,7 @@ def _token_worker(rank, world, port, name, peer, out_q):
         dist.all_gather(gathered, same)
         identical = all(torch.equal(g, same) for g in gathered)
         status = 0 if exchange is None else exchange.status()
-        out_q.put((rank, tracking(ref, ref_logits, two_logits), identical, status))
+        return tracking(ref, ref_logits, two_logits), identical, status
     finally:
         if exchange is not None:
             torch.cuda.synchronize()
@@ -266,17 +293,8 @@ def test_tensor_parallel_tokens_follow_tp1(name, peer):
     least 32 FP16 ulps; both ranks hold bit-identical logits."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_token_worker, args=(r, 2, port, name, peer, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=600) for _ in procs]
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    for rank, (drift, sure, bad, agree), identical, status in res:
+    res = _run_two_ranks(_token_worker, name, peer)
+    for rank, ((drift, sure, bad, agree), identical, status) in enumerate(res):
         print(f"{name} peer={peer} rank {rank}: drift {drift:.4f}, sure {sure:.2f}, agree {agree:.3f}, "
               f"differing picks {bad}")
         assert drift <= 0.06, (rank, drift)
