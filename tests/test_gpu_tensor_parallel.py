@@ -270,7 +270,7 @@ def _token_worker(rank, world, port, name, peer):
         tensor_parallel_(two, rank, world, lambda n, n_tr, n_tc: keep[n], cfg=cfg, model_type=spec["arch"],
                          exchange=exchange)
         _, two_logits = greedy_steps(two, prompt, dev, T.NEW_TOKENS, eager=False, forced=ref)
-        same = two_logits.view(torch.int16).to(dev)
+        same = two_logits.view(torch.int16).to(dev, torch.int32)  # the logits' bits; NCCL has no int16
         gathered = [torch.empty_like(same) for _ in range(world)]
         dist.all_gather(gathered, same)
         identical = all(torch.equal(g, same) for g in gathered)
