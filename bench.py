@@ -616,10 +616,11 @@ def run_prefill(args, ws, rank, device):
 
     line = {
         "metric": METRIC_PREFILL, "value": round(value, 2), "unit": "TOPS", "n_gpus": ws, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 (exact i32 tile products) + bf16, f32 accumulate",
         "data": "synthetic (seeded random init)",
-        "config": dict(PREFILL_CONFIG, parallelism=f"replicas x{ws}"),
+        "config": dict(PREFILL_CONFIG, parallelism="tp1: the whole block on one GPU (the N = 1 point of the "
+                                                   "tensor-parallel series run under torchrun)"),
         "roofline": {"kernel": "mixed GEMM, stacked gate/up (8192 x 16384 x 3072)", "bound": "tensor",
                      "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                      "frac": round(achieved / peak, 3), "peak_source": peak_src, "ops_per_launch": k_ops,
@@ -982,7 +983,7 @@ def run_reference(args, ws, rank):
     return {
         "impl": "reference", "metric": METRIC_PREFILL, "value": value, "unit": "TOPS", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 + bf16 (CPU)",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 + bf16 (CPU)",
         "data": "synthetic (seeded random init)",
         "config": dict(PREFILL_CONFIG, parallelism="one host, all cores"),
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
