@@ -108,3 +108,30 @@ def test_decoder_peer_status_raises_after_a_timeout():
     ex.word = N.TQ_ERR_TIMEOUT
     with pytest.raises(N.TileQuantError, match="reset the exchange"):
         dec.check_peer_status()
+
+
+def test_decoder_step_status_raises_and_clears_after_a_timeout():
+    """The fused decode step's attention error word is read at the same synchronised
+    point: a timed-out cache load surfaces as TileQuantError and the word is cleared."""
+    from tilequant_b200 import _native as N
+    from tilequant_b200.graph_decode import CudaGraphGreedyDecoder
+
+    class Step:  # the attention error word of a FusedDecodeStep
+        def __init__(self):
+            self.word = N.TQ_OK
+
+        def status(self):
+            return self.word
+
+        def reset_status(self):
+            self.word = N.TQ_OK
+
+    dec = CudaGraphGreedyDecoder.__new__(CudaGraphGreedyDecoder)
+    dec._step = None
+    dec.check_step_status()  # no fused step: nothing to read
+    dec._step = Step()
+    dec.check_step_status()
+    dec._step.word = N.TQ_ERR_TIMEOUT
+    with pytest.raises(N.TileQuantError, match="KV-cache chunk"):
+        dec.check_step_status()
+    dec.check_step_status()  # cleared

@@ -259,6 +259,10 @@ class FusedDecodeStep:
         """The attention kernel's error word (0, or TQ_ERR_TIMEOUT); synchronises."""
         return int(self.ws.err.item())
 
+    def reset_status(self) -> None:
+        """Clear the attention kernel's error word (stream-ordered)."""
+        self.ws.err.zero_()
+
     @traced("tq.FusedDecodeStep")
     @torch.inference_mode()
     def __call__(self, token: torch.Tensor, position: torch.Tensor) -> torch.Tensor:

@@ -359,7 +359,24 @@ class CudaGraphGreedyDecoder:
         torch.cuda.synchronize(self.device)
         end = time.perf_counter()
         self.check_peer_status()
+        self.check_step_status()
         return ids, GreedyGenerationTiming(start, first, end)
+
+    def check_step_status(self) -> None:
+        """Raise ``TileQuantError`` if a bounded wait of the fused decode step's attention
+        kernel gave up (a chunk of the KV cache never reached shared memory, so that
+        step's logits, and the ids after it, are undefined).  Reads the step's error word,
+        which synchronises, and clears it; no-op without a fused step."""
+        from ._native import TQ_OK, TileQuantError
+
+        step = getattr(self, "_step", None)
+        if step is None:
+            return
+        st = step.status()
+        if st != TQ_OK:
+            step.reset_status()
+            raise TileQuantError(f"decode attention: a wait for a KV-cache chunk ran out (status {st}); the "
+                                 "request's ids are undefined")
 
     def check_peer_status(self) -> None:
         """Raise ``TileQuantError`` if a row-parallel peer sum of the model gave up
