@@ -143,7 +143,7 @@ TQ_API int tq_gemm_mixed_fused_quant(const void* x_fp, int64_t ld_xfp, int fp_dt
                               int64_t k, int n_tr, int n_tc, int split_k, int* err, void* stream);
 
 /* Launch geometry the decode kernels use when split_k = 0 on this device: *split
- * (1..16) and *rows_per_cta (row tiles one CTA streams when split is 1).  Up to 16 rows
+ * (1..16) and *rows_per_cta (row tiles one CTA streams when split is 1).
  * Up to 8 rows (with or without fused quantization) this is the split of TQ_ALGO_STREAM:
  * the most splits (at most 8, at least 4 INT8 tiles each) whose n_tr clusters of split
  * CTAs are all resident on this device at once, 1 if none is; the automatic choice also
