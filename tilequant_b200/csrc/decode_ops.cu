@@ -388,13 +388,19 @@ __global__ void __launch_bounds__(at::WARPS * 32) attn_partial_kernel(const Attn
         mma_16816<XT>(o[2 * jp + 1], pa0, 0u, pa2, 0u, r[2], r[3]);
       }
     }
-    __syncthreads();  // every warp is done with this stage
-    if (tid == 0 && ok && ci + NSTG < nch) issue(ci + NSTG);
+    // a stage is refilled only when a later chunk goes into it (ci + NSTG < nch, the same
+    // for every thread): only then must every warp be done with it first
+    if (ci + NSTG < nch) {
+      __syncthreads();
+      if (tid == 0 && ok) issue(ci + NSTG);
+    }
   }
   l_part += __shfl_xor_sync(0xffffffffu, l_part, 1);
   l_part += __shfl_xor_sync(0xffffffffu, l_part, 2);
 
-  // merge the four warps (their stage memory is free now: every load issued was awaited)
+  // merge the four warps in the K stages: every load issued was awaited, and after this
+  // barrier no warp still reads a stage
+  __syncthreads();
   float* mrg_o = reinterpret_cast<float*>(ks);  // WARPS x MAXG x D
   if (g < G) {
     if (t == 0) {
