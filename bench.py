@@ -352,13 +352,16 @@ def _cpu_sample(linears, rows: int, window: int = 0):
 
 def _cpu_baseline_line(linears, rows: int, seconds: float):
     """Windows of `rows` rows through the four linears, repeated for about `seconds`."""
+    from oracle import oracle as O
+
+    threads = O.set_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     spent, ops, w = 0.0, 0, 0
     while spent < seconds or w < 1:
         s, o = _cpu_sample(linears, rows, w)
         spent += s
         ops += o
         w += 1
-    return {"value": ops / spent / 1e12, "unit": "TOPS", "cores": os.cpu_count() or 1, "kind": "port",
+    return {"value": ops / spent / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
             "sample": f"{w} windows of {rows} consecutive rows (of 8192) through the 4 config-2 linears, each window "
                       "quantized and multiplied as one call by oracle/tq_oracle.c (the reference's arithmetic, "
                       "OpenMP on all host threads); weights and tile maps as the GPU run, seeded N(0,1) inputs"}
@@ -657,6 +660,7 @@ def decode_cpu_baseline(x, w, fp16, int8, n_tr, n_tc, bytes_per_call, seconds=3.
     xb = I.bits(x)
     pk = O.pack(I.bits(w), n_tr, n_tc, int8.numpy(), fp16.numpy())
     m, k = w.shape
+    threads = O.set_threads(os.cpu_count() or 1)  # all host threads, whatever the launcher set
     q, sx = O.quantize_act(xb)  # warm-up (loads the library, touches the arrays)
     O.gemm(q, sx, pk, xb, m, k, split_k=1)
     calls, spent = 0, 0.0
@@ -666,7 +670,7 @@ def decode_cpu_baseline(x, w, fp16, int8, n_tr, n_tc, bytes_per_call, seconds=3.
         O.gemm(q, sx, pk, xb, m, k, split_k=1)
         spent += time.perf_counter() - t0
         calls += 1
-    return {"value": round(bytes_per_call * calls / spent / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count() or 1,
+    return {"value": round(bytes_per_call * calls / spent / 1e9, 3), "unit": "GB/s", "cores": threads,
             "kind": "port", "sample": f"{calls} whole config-1 calls (quantize 16 x {k} + mixed GEMM {m} x {k}) through "
                                       "oracle/tq_oracle.c (OpenMP)"}
 
@@ -967,6 +971,10 @@ def run_reference(args, ws, rank):
     quantized and multiplied as one call."""
     if rank != 0:
         return None
+    from oracle import oracle as O
+
+    # all host threads: torchrun hands every rank OMP_NUM_THREADS=1, and rank 0 runs alone
+    threads = O.set_threads(os.cpu_count() or 1)
     linears = _reference_linears()
     for w in range(args.warmup):
         _cpu_sample(linears, args.cpu_rows, w)
@@ -976,7 +984,6 @@ def run_reference(args, ws, rank):
         secs += s
         ops += o
     value = ops / secs / 1e12
-    threads = os.cpu_count() or 1
     sample = (f"per step one window of {args.cpu_rows} consecutive rows (of 8192) through the 4 config-2 linears, "
               "quantized and multiplied as one call by oracle/tq_oracle.c (OpenMP, all host threads); weights and "
               "tile maps as the GPU run (same seeds), seeded N(0,1) inputs")

@@ -65,11 +65,20 @@ def lib():
         L.tqo_calib_gi_accumulate.argtypes = [P, P, I, I64, I64, I, I, P]
         L.tqo_iaa_channel_accumulate.argtypes = [P, I, I64, I64, P]
         L.tqo_iaa_tile_scores.argtypes = [P, I, I64, I64, I, I, P, I64, P, P]
+        L.tqo_set_threads.argtypes = [I]
+        L.tqo_set_threads.restype = I
         for fn in ("tqo_act_scales", "tqo_quantize_with_scales", "tqo_pack_int8", "tqo_gemm_mixed",
                    "tqo_calib_gi_accumulate", "tqo_iaa_channel_accumulate", "tqo_iaa_tile_scores"):
             getattr(L, fn).restype = None
         _lib = L
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """Threads of the restatement's OpenMP loops on the calling thread (whatever
+    OMP_NUM_THREADS the process inherited, e.g. 1 under torchrun); returns the count
+    its next loop will use."""
+    return int(lib().tqo_set_threads(int(n)))
 
 
 def _ptr(a):

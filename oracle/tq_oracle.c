@@ -25,9 +25,25 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 #define TQO_BF16 0
 #define TQO_F16 1
+
+/* Threads of the OpenMP loops of the calling thread (n > 0 sets them, whatever
+ * OMP_NUM_THREADS the process inherited; n <= 0 leaves them); returns the count the
+ * next parallel loop will use. */
+int tqo_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
 
 /* ---------------------------------------------------------------- 16-bit floats */
 
