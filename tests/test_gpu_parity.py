@@ -74,6 +74,26 @@ def test_quantizer_rejects_bad_input(cuda_device):
         tq.quantize_activation_tile_absmax(torch.zeros(4, 64, dtype=torch.bfloat16))  # CPU tensor
 
 
+def test_empty_batch_follows_the_reference(cuda_device):
+    """Zero rows: the unfused scales raise as the reference's amax over an empty dimension
+    does (quant_utils.py:68-69); the fused quantizer gives no codes and scale 1.0 per tile,
+    as the reference's fused kernel reducing over no rows does (quantize_activation.py:
+    100-106); codes with given scales, the GEMM and MixedLinear return empty outputs."""
+    x = torch.empty((0, 200), device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(IndexError):
+        tq.activation_tile_absmax_scales(x)
+    q, sx = tq.quantize_activation_tile_absmax(x)
+    torch.cuda.synchronize()
+    assert q.shape == (0, 200) and q.dtype == torch.int8
+    assert torch.equal(sx.cpu(), torch.ones(4))
+    assert tq.quantize_activation_tile_with_scales(x, sx).shape == (0, 200)
+    lin, *_ = _linear(128, 200, 0.1, 5)
+    with torch.inference_mode():
+        y = lin(x)
+        y3 = lin(torch.empty((2, 0, 200), device=DEV, dtype=torch.bfloat16))
+    assert y.shape == (0, 128) and y3.shape == (2, 0, 128)
+
+
 # ---------------------------------------------------------------------- packer
 
 @pytest.mark.parametrize("name", _cases(PACK, "__in_int8_ids"))

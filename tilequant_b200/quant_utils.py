@@ -39,13 +39,18 @@ def _check_2d(x_fp: torch.Tensor, tile_n: int) -> None:
 
 
 def activation_tile_absmax_scales(x_fp: torch.Tensor, tile_n: int = 64) -> torch.Tensor:
-    """f32[n_tc] scales of the 64-column tiles of ``x_fp`` (quant_utils.py:41-74)."""
+    """f32[n_tc] scales of the 64-column tiles of ``x_fp`` (quant_utils.py:41-74).  Zero
+    rows with columns raise IndexError, as the reference's amax over the empty row
+    dimension does (quant_utils.py:68-69); ``quantize_activation_tile_absmax`` instead
+    gives scale 1.0 per tile there, like the reference's fused kernel."""
     _check_2d(x_fp, tile_n)
     n, k = x_fp.shape
     n_tc = (int(k) + TILE - 1) // TILE
     sx = torch.empty((n_tc,), device=x_fp.device, dtype=torch.float32)
     if k == 0:
         return sx
+    if n == 0:
+        raise IndexError("activation_tile_absmax_scales: x has no rows (a maximum over an empty dimension)")
     rc = N.load().tq_act_scales(x_fp.data_ptr(), N.dtype_code(x_fp.dtype), int(n), int(k), x_fp.stride(0),
                                 x_fp.stride(1), sx.data_ptr(), N.stream_of(x_fp))
     N.check(rc, "activation_tile_absmax_scales")
