@@ -52,6 +52,30 @@
 
 namespace tq {
 
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok)
+               : "r"(smem_u32(bar)), "r"(parity)
+               : "memory");
+  return ok != 0;
+}
+
+// Spin on an mbarrier phase without suspending, bounded by about two seconds (then
+// TQ_ERR_TIMEOUT).  Used for the MMA <-> epilogue hand-offs, whose wake-up latency is
+// on the kernel's critical path (1-1.5 % faster than the sleeping wait on the prefill
+// shapes); the other roles keep the sleeping wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err) {
+  const uint64_t t0 = global_ns();
+#pragma unroll 1
+  for (uint32_t i = 0; i < (1u << 31); ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && global_ns() - t0 > kWaitLimitNs) break;
+  }
+  report(err, TQ_ERR_TIMEOUT);
+  return false;
+}
+
 namespace um {
 constexpr int BM = 128;             // activation rows per output tile (MMA M)
 constexpr int A_BYTES = BM * 64;    // 8 KB activation tile of one K step
@@ -423,8 +447,8 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
           for (int c0 = 0; c0 < n_tc; c0 += GS, ++g, ++grp) {
             const int stg = g % NS, ns = min(GS, n_tc - c0);
             const uint32_t gb = grp % NG;
-            if (ok && !mbar_wait_sleep(&full[stg], (g / NS) & 1, a.err)) ok = false;
-            if (ok && !mbar_wait_sleep(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait_spin(&full[stg], (g / NS) & 1, a.err)) ok = false;
+            if (ok && !mbar_wait_spin(&tempty[gb], (grp / NG) & 1, a.err)) ok = false;
             tc_fence_after();
             for (int s = 0; s < ns; ++s) {
               const uint32_t sa = smem_u32(stages + stg * STAGE + s * STEP_BYTES);
@@ -513,7 +537,7 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
             pp[s][t] = DUMP && in ? pos[t * n_tc + c0 + s] : -1;
           }
         const uint32_t t0 = tbase + gb * GS * BN;  // step s, chunk u at t0 + s * BN + u * CH
-        if (ok && !mbar_wait_sleep(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
+        if (ok && !mbar_wait_spin(&tfull[gb], (grp / NG) & 1, a.err)) ok = false;
         tc_fence_after();
         // CH-column chunks (step s = i / CPS, columns CH * (i % CPS)), each chunk's load
         // issued before the previous chunk's rescale so the TMEM latency overlaps FP work
