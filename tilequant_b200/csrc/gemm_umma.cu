@@ -548,7 +548,6 @@ __global__ void __launch_bounds__(um::THREADS, 1) umma_kernel(const RowsArgs a, 
 #pragma unroll
         for (int i = 0; i < GS * CPS; ++i) {
           const int s = i / CPS, cc = (i % CPS) * CH, t = cc >> 6;
-          const uint32_t ti = t0 + s * BN + cc;
           if (i + 1 < GS * CPS) tmem_ld_chunk<CH>(t0 + ((i + 1) / CPS) * BN + ((i + 1) % CPS) * CH, v[(i + 1) & 1]);
 #pragma unroll
           for (int hh = 0; hh < CH / 16; ++hh) {
