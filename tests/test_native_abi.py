@@ -95,3 +95,25 @@ def test_python_errors_map_to_reference_exceptions(lib):
         N.check(N.TQ_ERR_INVALID, "x")
     with pytest.raises(N.TileQuantError):
         N.check(N.TQ_ERR_CUDA, "x")
+
+
+def test_integration_binding_matches_the_library():
+    """The ctypes binding shown to maintainers names every
+    entry point of the header and gives each the argument count and types this
+    package's own binding uses."""
+    doc = (ROOT / "INTEGRATION.md").read_text()
+    start = doc.index("```python", doc.index("## 2."))
+    block = doc[start:doc.index("```", start + 10)]
+    block = re.sub(r"\[\s*([^\]]*?)\]", lambda m: "[" + " ".join(m.group(1).split()) + "]", block, flags=re.S)
+    for name in _declared():
+        assert name in doc, f"{name} missing from the integration guide"
+    kinds = {"P": ctypes.c_void_p, "I64": ctypes.c_int64, "I": ctypes.c_int, "F": ctypes.c_float}
+    bound = re.findall(r"lib\.(tq_\w+)\.argtypes = \[([^\]]*)\]", block)
+    assert len(bound) >= 20
+    for name, args in bound:
+        args = [a.strip() for a in args.split(",") if a.strip()]
+        want = N.SIGNATURES[name]
+        assert len(args) == len(want), (name, len(args), len(want))
+        for i, (a, w) in enumerate(zip(args, want)):
+            if a in kinds:
+                assert kinds[a] is w, (name, i, a, w)
