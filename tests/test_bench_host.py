@@ -3,6 +3,7 @@ restatement of the reference, timed on the host cores) and the argument surface.
 
 from __future__ import annotations
 
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -30,12 +31,16 @@ def test_bench_help_lists_the_workloads():
 
 
 def test_reference_arm_is_host_only():
-    """The reference arm times the CPU restatement without this project's GPU library."""
-    code = ("import sys, types, bench; "
+    """The reference arm times the CPU restatement without this project's GPU library,
+    on every host thread even when launched with OMP_NUM_THREADS=1 (as torchrun starts
+    each rank)."""
+    code = ("import os, sys, types, bench; "
             "a = types.SimpleNamespace(steps=1, warmup=0, cpu_rows=4); "
             "line = bench.run_reference(a, 1, 0); "
             "assert line['impl'] == 'reference' and line['value'] > 0, line; "
             "assert line['config'] == dict(bench.PREFILL_CONFIG, parallelism='one host, all cores'); "
+            "assert line['cpu_baseline']['cores'] == (os.cpu_count() or 1), line['cpu_baseline']; "
             "assert 'tilequant_b200' not in sys.modules, 'GPU library imported'; print('ok')")
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=ROOT, timeout=600)
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=ROOT, timeout=600, env=env)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
