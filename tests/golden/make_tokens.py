@@ -31,7 +31,6 @@ test can check it rebuilt the same model.
 
 from __future__ import annotations
 
-import hashlib
 import os
 import sys
 import time
