@@ -117,3 +117,38 @@ def test_integration_binding_matches_the_library():
         for i, (a, w) in enumerate(zip(args, want)):
             if a in kinds:
                 assert kinds[a] is w, (name, i, a, w)
+
+
+def test_decode_step_entries_check_arguments_on_the_host(lib):
+    """The decode-step entry points reject bad calls before any CUDA call (fake,
+    never-dereferenced pointers stand in for device memory)."""
+    d, odd = ctypes.c_void_p(4096), ctypes.c_void_p(4096 + 8)
+    # residual add + RMSNorm: dtype, width, null operands, strides, alignment; zero rows is a no-op
+    assert lib.tq_add_rmsnorm(d, 64, None, 0, d, None, 0, d, 64, 2, 64, 1e-6, 7, None) == N.TQ_ERR_INVALID
+    assert lib.tq_add_rmsnorm(d, 64, None, 0, d, None, 0, d, 64, 2, 60, 1e-6, 0, None) == N.TQ_ERR_INVALID
+    assert b"multiple of 8" in lib.tq_last_error()
+    assert lib.tq_add_rmsnorm(d, 64, None, 0, d, None, 0, d, 64, 0, 64, 1e-6, 0, None) == N.TQ_OK
+    assert lib.tq_add_rmsnorm(None, 64, None, 0, d, None, 0, d, 64, 2, 64, 1e-6, 0, None) == N.TQ_ERR_INVALID
+    assert lib.tq_add_rmsnorm(d, 64, d, 64, d, None, 0, d, 64, 2, 64, 1e-6, 0, None) == N.TQ_ERR_INVALID  # no resid_out
+    assert lib.tq_add_rmsnorm(d, 32, None, 0, d, None, 0, d, 64, 2, 64, 1e-6, 0, None) == N.TQ_ERR_INVALID
+    assert b"row stride" in lib.tq_last_error()
+    assert lib.tq_add_rmsnorm(odd, 64, None, 0, d, None, 0, d, 64, 2, 64, 1e-6, 0, None) == N.TQ_ERR_INVALID
+    assert b"16-byte" in lib.tq_last_error()
+    # SiLU * up + quantizer: at most 128 rows, strides at least k
+    assert lib.tq_silu_mul_quant(d, d, 64, 129, 64, d, 64, d, 64, d, 0, None) == N.TQ_ERR_INVALID
+    assert lib.tq_silu_mul_quant(d, d, 32, 4, 64, d, 64, d, 64, d, 0, None) == N.TQ_ERR_INVALID
+    # decode attention: head_dim, heads per KV head, cache length, alignment
+    a = N.AttnArgs(q=4096, k=4096, v=4096, cos=4096, sin=4096, k_cache=4096, v_cache=4096, pos=4096, ws_m=4096,
+                   ws_l=4096, ws_o=4096, err=0, ld_q=1024, ld_k=256, ld_v=256, B=4, Hq=8, Hkv=2, D=128, L=64, S=2,
+                   scale_log2=0.1, reserved=0)
+    assert lib.tq_attn_decode(None, d, 1024, None, 0, None, 0, None) == N.TQ_ERR_INVALID
+    for field, value, code in (("D", 96, N.TQ_ERR_UNSUPPORTED), ("Hq", 32, N.TQ_ERR_UNSUPPORTED),
+                               ("L", 0, N.TQ_ERR_INVALID), ("k_cache", 4104, N.TQ_ERR_INVALID),
+                               ("ld_q", 1020, N.TQ_ERR_INVALID)):
+        bad = N.AttnArgs.from_buffer_copy(a)
+        setattr(bad, field, value)
+        assert lib.tq_attn_decode(ctypes.byref(bad), d, 1024, None, 0, None, 0, None) == code, field
+    assert lib.tq_attn_decode(ctypes.byref(a), d, 512, None, 0, None, 0, None) == N.TQ_ERR_INVALID  # ld_out < Hq*D
+    # greedy pick: row count, vocabulary within the row stride
+    assert lib.tq_greedy_pick(d, 128, 0, 128, 0, d, None, None, None, 0, 0, d, 0, None) == N.TQ_ERR_INVALID
+    assert lib.tq_greedy_pick(d, 100, 2, 128, 0, d, None, None, None, 0, 0, d, 0, None) == N.TQ_ERR_INVALID
